@@ -1,0 +1,171 @@
+// Host-side launch interfaces shared by the kernel files and the C ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/adaattn_b200.h"
+
+namespace ada {
+
+// --- analyzer ---------------------------------------------------------------
+struct AnalyzeLaunch {
+    const void* q;
+    const void* k;
+    int dtype;
+    int64_t B, H, Nq, Nk, D;
+    int64_t qs[4], ks[4];
+    float scale, eps;
+    double log_s;
+    int S, stride;
+    float* head_stats;
+    float* head_sum;
+    int32_t* decisions;
+    float* summary;
+    double rank_threshold;
+    int enable_rank, enable_prec, default_prec, allow_fp8, granularity;
+};
+int launch_analyze(const AnalyzeLaunch& L, cudaStream_t stream);
+int launch_entropy_rows(const void* w, int dtype, int64_t rows, int64_t len, float* out,
+                        cudaStream_t stream);
+int launch_effective_rank(const void* w, int dtype, int64_t groups, int64_t group, int64_t len,
+                          float* out, cudaStream_t stream);
+int launch_target_ranks(const float* eff, int64_t n, int64_t min_rank, int64_t max_rank, double thr,
+                        int64_t* out, cudaStream_t stream);
+int launch_bounded_wait(uint64_t timeout_ns, unsigned int* status, cudaStream_t stream);
+
+// --- which heads a launch serves ---------------------------------------------
+// A head (b,h) is served when decisions == nullptr (static decision) or when
+// its precision code is in prec_mask and its low-rank flag equals low_rank.
+struct HeadSelect {
+    const int32_t* decisions;
+    uint32_t prec_mask;
+    int low_rank;
+};
+
+__host__ __device__ inline bool head_selected(const HeadSelect& s, int64_t bh) {
+#ifdef __CUDA_ARCH__
+    if (s.decisions == nullptr) return true;
+    const int p = s.decisions[bh * 2 + 0];
+    const int l = s.decisions[bh * 2 + 1];
+    return ((s.prec_mask >> p) & 1u) && (l != 0) == (s.low_rank != 0);
+#else
+    (void)s;
+    (void)bh;
+    return true;
+#endif
+}
+
+// Optional additive / boolean mask, broadcast view over [B, H, Nq, Nk].
+struct MaskView {
+    const void* data;  // nullptr: no mask
+    int dtype;         // ADA_BOOL or a float type
+    int64_t s[4];
+};
+
+// --- operand preparation (casts, low-rank projection, E4M3 quantisation) ----
+// Where each (b,h) slice's decision comes from.
+struct DecisionSrc {
+    const int32_t* decisions;  // [B*H*2] or nullptr
+    int static_prec, static_low;
+};
+
+__host__ __device__ inline void get_decision(const DecisionSrc& d, int64_t bh, int* prec, int* low) {
+    if (d.decisions != nullptr) {
+        *prec = d.decisions[bh * 2 + 0];
+        *low = d.decisions[bh * 2 + 1];
+    } else {
+        *prec = d.static_prec;
+        *low = d.static_low;
+    }
+}
+
+struct PrepLaunch {
+    DecisionSrc dec;
+    // inputs [B,H,N,D]
+    const void* q;
+    const void* k;
+    const void* v;
+    int in_dtype;
+    int64_t B, H, Nq, Nk, D;
+    int64_t qs[4], ks[4], vs[4];
+    const void* w_down;  // [r, D] row-major contiguous, or nullptr
+    int w_dtype;
+    int64_t r;
+    // 16-bit region: heads of the 16-bit tensor-core precisions that cannot be
+    // read in place (dtype change, low rank, or layout) -- [B,H,N,ld]
+    uint32_t tc16_mask;   // precision codes served by the 16-bit kernels
+    uint32_t f16_mask;    // ...of which these compute in fp16 (the rest bf16)
+    int direct_ok;        // dense heads already in their compute dtype are read in place
+    void* ws16_q;
+    void* ws16_k;
+    void* ws16_v;
+    int64_t ld16_qk, ld16_v;
+    int dqk_dense, dqk_low, dv_pad;  // padded widths written (zero filled)
+    // fp32 region for FP32 low-rank heads: q_low/k_low [B,H,N,r]
+    uint32_t fp32_mask;
+    float* ws32_q;
+    float* ws32_k;
+    // e4m3 region [B,H,N,128] plus per-tile scales
+    uint32_t fp8_mask;
+    uint8_t* ws8_q;
+    uint8_t* ws8_k;
+    uint8_t* ws8_v;
+    float* amax_q;  // [B,H,nt_q]
+    float* amax_k;  // [B,H,nt_k]
+    float* amax_v;  // [B,H,nt_k]
+    float* scale_q; // [B,H,nt_q]
+    float* scale_k; // [B,H,nt_k]
+    float* scale_v; // [B,H]
+    int64_t nt_q, nt_k;
+};
+int launch_prep16(const PrepLaunch& L, cudaStream_t stream);
+int launch_prep32(const PrepLaunch& L, cudaStream_t stream);
+int launch_prep8(const PrepLaunch& L, cudaStream_t stream);
+
+// --- tensor-core FMHA (tcgen05) -----------------------------------------------
+struct TcLaunch {
+    CUtensorMap tq, tk, tv;
+    int elt;          // 0 f16, 1 bf16, 2 e4m3
+    int dqk, dv;      // operand widths (64 or 128)
+    int64_t B, H, Nq, Nk;
+    int dv_out;       // real value width stored
+    void* out;
+    int out_dtype;
+    int64_t os[4];
+    int out_vec;      // 1: 16-byte vector stores are aligned
+    int round_dtype;  // dtype the reference's result has before its cast back
+    float scale_log2; // softmax scale * log2(e)
+    int causal;
+    MaskView mask;
+    HeadSelect sel;
+    const float* q_scale;  // e4m3: [B,H,nt_q]
+    const float* k_scale;  // e4m3: [B,H,nt_k]
+    const float* v_scale;  // e4m3: [B,H]
+    int64_t nt_q, nt_k;
+    unsigned int* status;
+    uint64_t timeout_ns;
+};
+int launch_fmha_tc(const TcLaunch& L, cudaStream_t stream);
+
+// --- fp32 SIMT FMHA ----------------------------------------------------------
+struct SimtLaunch {
+    const void* q;   // [B,H,Nq,dqk] (q or q_low)
+    const void* k;
+    const void* v;   // [B,H,Nk,dv]
+    int q_dtype, k_dtype, v_dtype;
+    int64_t qs[4], ks[4], vs[4];
+    int64_t B, H, Nq, Nk;
+    int dqk, dv;
+    void* out;
+    int out_dtype;
+    int64_t os[4];
+    float scale;
+    int causal;
+    MaskView mask;
+    HeadSelect sel;
+};
+int launch_fmha_simt(const SimtLaunch& L, cudaStream_t stream);
+
+}  // namespace ada

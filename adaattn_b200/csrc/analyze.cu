@@ -1,0 +1,426 @@
+// K1: the runtime analyzer. One CTA per (b, h) computes the statistics of the
+// sampled score block, then one CTA turns them into decisions, per head or
+// for the whole call. Restates src/adaattn/attention/adaattn.py:246-289.
+//
+// Every intermediate is rounded to the inputs' dtype exactly where the
+// reference's PyTorch ops produce a tensor of that dtype (matmul output,
+// scaled scores, softmax output, p + eps, log, p * log, row sums, the
+// normalised entropy and its mean), so decisions agree with the reference
+// except where a statistic sits within rounding distance of a threshold.
+#include "ada_common.cuh"
+#include "ada_internal.h"
+
+namespace ada {
+
+namespace {
+
+constexpr int kSample = 64;
+constexpr int kThreads = 256;
+
+struct StatsArgs {
+    const void* q;
+    const void* k;
+    int dtype;
+    int64_t B, H, Nq, Nk, D;
+    int64_t qs[4], ks[4];
+    float scale, eps, log_s;
+    int S, stride;
+    float* head_stats;  // [B*H*4]
+    float* head_sum;    // [B*H]  sum over sampled rows of the normalised row entropy
+};
+
+__global__ void __launch_bounds__(kThreads) analyze_stats_kernel(StatsArgs a) {
+    extern __shared__ float sm[];
+    const int D = static_cast<int>(a.D);
+    const int ld = D + 1;
+    float* sq = sm;
+    float* sk = sm + kSample * ld;
+    __shared__ unsigned int s_max_score, s_max_prob;
+    __shared__ float s_rows[kSample];
+
+    const int bh = blockIdx.x;
+    const int b = bh / static_cast<int>(a.H);
+    const int h = bh % static_cast<int>(a.H);
+    const int tid = threadIdx.x;
+    const int S = a.S;
+    if (tid == 0) {
+        s_max_score = 0u;
+        s_max_prob = 0u;
+    }
+    const int64_t qbase = b * a.qs[0] + h * a.qs[1];
+    const int64_t kbase = b * a.ks[0] + h * a.ks[1];
+    for (int idx = tid; idx < S * D; idx += kThreads) {
+        const int r = idx / D, d = idx - r * D;
+        const int64_t row = static_cast<int64_t>(r) * a.stride;
+        sq[r * ld + d] = load_as_f32(a.q, qbase + row * a.qs[2] + d * a.qs[3], a.dtype);
+        sk[r * ld + d] = load_as_f32(a.k, kbase + row * a.ks[2] + d * a.ks[3], a.dtype);
+    }
+    __syncthreads();
+
+    // Thread layout: 4 consecutive lanes own one sample row, 16 columns each.
+    const int r = tid >> 2;
+    const int c0 = (tid & 3) * 16;
+    const bool row_ok = r < S;
+    float sc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) sc[j] = 0.f;
+    if (row_ok) {
+        const float* qr = sq + r * ld;
+        for (int d = 0; d < D; ++d) {
+            const float qv = qr[d];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int col = c0 + j;
+                if (col < S) sc[j] = fmaf(qv, sk[col * ld + d], sc[j]);
+            }
+        }
+    }
+    // scores = round(round(q k^T) * scale); track max |score|.
+    float local_max_abs = 0.f;
+    float row_max = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const bool ok = row_ok && (c0 + j) < S;
+        float s = round_to(round_to(sc[j], a.dtype) * a.scale, a.dtype);
+        sc[j] = ok ? s : -INFINITY;
+        if (ok) {
+            local_max_abs = fmaxf(local_max_abs, fabsf(s));
+            row_max = fmaxf(row_max, s);
+        }
+    }
+    row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, 1));
+    row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, 2));
+    // softmax in fp32 on the rounded scores, output rounded to the dtype.
+    float e[16];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        e[j] = (sc[j] == -INFINITY) ? 0.f : expf(sc[j] - row_max);
+        sum += e[j];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    const float inv = 1.f / sum;
+    float local_max_prob = 0.f;
+    float ent = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        if (row_ok && (c0 + j) < S) {
+            const float p = round_to(e[j] * inv, a.dtype);
+            local_max_prob = fmaxf(local_max_prob, p);
+            const float t1 = round_to(p + a.eps, a.dtype);
+            const float t2 = round_to(logf(t1), a.dtype);
+            ent += round_to(p * t2, a.dtype);
+        }
+    }
+    ent += __shfl_xor_sync(0xffffffffu, ent, 1);
+    ent += __shfl_xor_sync(0xffffffffu, ent, 2);
+    if (row_ok && (tid & 3) == 0) {
+        const float row_entropy = -round_to(ent, a.dtype);
+        s_rows[r] = round_to(row_entropy / a.log_s, a.dtype);
+    }
+    // block maxima (non-negative floats compare like their bit patterns)
+    for (int o = 16; o > 0; o >>= 1) {
+        local_max_abs = fmaxf(local_max_abs, __shfl_xor_sync(0xffffffffu, local_max_abs, o));
+        local_max_prob = fmaxf(local_max_prob, __shfl_xor_sync(0xffffffffu, local_max_prob, o));
+    }
+    __syncthreads();
+    if ((tid & 31) == 0) {
+        atomicMax(&s_max_score, __float_as_uint(local_max_abs));
+        atomicMax(&s_max_prob, __float_as_uint(local_max_prob));
+    }
+    __syncthreads();
+    if (tid < 32) {
+        float v = 0.f;
+        for (int i = tid; i < S; i += 32) v += s_rows[i];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (tid == 0) {
+            const float ne = round_to(v / static_cast<float>(S), a.dtype);
+            float* hs = a.head_stats + static_cast<int64_t>(bh) * 4;
+            hs[0] = ne;
+            hs[1] = __uint_as_float(s_max_score);
+            hs[2] = __uint_as_float(s_max_prob);
+            hs[3] = ne * static_cast<float>(a.Nq < a.Nk ? a.Nq : a.Nk);
+            a.head_sum[bh] = v;
+        }
+    }
+}
+
+struct DecideArgs {
+    const float* head_stats;
+    const float* head_sum;
+    int32_t* decisions;
+    float* summary;
+    int64_t BH;
+    int S;
+    int dtype;
+    int64_t min_n;
+    double rank_threshold;
+    int enable_rank, enable_prec, default_prec, allow_fp8, granularity;
+};
+
+__device__ __forceinline__ void decide_one(double ne, double ms, double mp, const DecideArgs& a,
+                                           int* prec, int* low) {
+    // adaattn.py:268-287, compared in double as the reference's Python floats are.
+    *low = (a.enable_rank && ne < a.rank_threshold) ? 1 : 0;
+    int p;
+    if (ms > 50.0 || mp > 0.95)
+        p = ADA_PREC_FP32;
+    else if (ne > 0.8)
+        p = a.allow_fp8 ? ADA_PREC_FP8 : ADA_PREC_FP16;
+    else if (ne < 0.3)
+        p = ADA_PREC_BF16;
+    else
+        p = a.default_prec;
+    if (!a.enable_prec) p = a.default_prec;
+    *prec = p;
+}
+
+__device__ __forceinline__ int prec_slot(int p) {
+    // _precision_distribution index; AUTO falls in slot 0 (.get(precision, 0)).
+    return (p >= ADA_PREC_FP32 && p <= ADA_PREC_FP8) ? p : 0;
+}
+
+__global__ void __launch_bounds__(kThreads) decide_kernel(DecideArgs a) {
+    __shared__ float s_sum[kThreads / 32];
+    __shared__ unsigned int s_ms, s_mp;
+    __shared__ int s_cnt[5];
+    const int tid = threadIdx.x;
+    if (tid < 5) s_cnt[tid] = 0;
+    if (tid == 0) {
+        s_ms = 0u;
+        s_mp = 0u;
+    }
+    __syncthreads();
+    if (a.granularity == 0) {
+        for (int64_t i = tid; i < a.BH; i += kThreads) {
+            const float* hs = a.head_stats + i * 4;
+            int p, low;
+            decide_one(hs[0], hs[1], hs[2], a, &p, &low);
+            a.decisions[i * 2 + 0] = p;
+            a.decisions[i * 2 + 1] = low;
+            atomicAdd(&s_cnt[prec_slot(p)], 1);
+            if (low) atomicAdd(&s_cnt[4], 1);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            a.summary[ADA_SUM_NE] = NAN;
+            a.summary[ADA_SUM_MAX_SCORE] = NAN;
+            a.summary[ADA_SUM_MAX_PROB] = NAN;
+            a.summary[ADA_SUM_EFF_RANK] = NAN;
+            a.summary[ADA_SUM_N_LOWRANK] = static_cast<float>(s_cnt[4]);
+            for (int i = 0; i < 4; ++i) a.summary[ADA_SUM_N_FP32 + i] = static_cast<float>(s_cnt[i]);
+            a.summary[ADA_SUM_N_TOTAL] = static_cast<float>(a.BH);
+        }
+        return;
+    }
+    // One decision for the whole call: mean of every sampled row's normalised
+    // entropy over all heads, maxima over all heads.
+    float v = 0.f, ms = 0.f, mp = 0.f;
+    for (int64_t i = tid; i < a.BH; i += kThreads) {
+        v += a.head_sum[i];
+        ms = fmaxf(ms, a.head_stats[i * 4 + 1]);
+        mp = fmaxf(mp, a.head_stats[i * 4 + 2]);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        v += __shfl_xor_sync(0xffffffffu, v, o);
+        ms = fmaxf(ms, __shfl_xor_sync(0xffffffffu, ms, o));
+        mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, o));
+    }
+    if ((tid & 31) == 0) {
+        s_sum[tid >> 5] = v;
+        atomicMax(&s_ms, __float_as_uint(ms));
+        atomicMax(&s_mp, __float_as_uint(mp));
+    }
+    __syncthreads();
+    __shared__ int s_dec[2];
+    __shared__ float s_ne;
+    if (tid == 0) {
+        float tot = 0.f;
+        for (int i = 0; i < kThreads / 32; ++i) tot += s_sum[i];
+        const float ne =
+            round_to(tot / static_cast<float>(static_cast<double>(a.BH) * a.S), a.dtype);
+        int p, low;
+        decide_one(ne, __uint_as_float(s_ms), __uint_as_float(s_mp), a, &p, &low);
+        s_dec[0] = p;
+        s_dec[1] = low;
+        s_ne = ne;
+        a.summary[ADA_SUM_NE] = ne;
+        a.summary[ADA_SUM_MAX_SCORE] = __uint_as_float(s_ms);
+        a.summary[ADA_SUM_MAX_PROB] = __uint_as_float(s_mp);
+        a.summary[ADA_SUM_EFF_RANK] = ne * static_cast<float>(a.min_n);
+        a.summary[ADA_SUM_N_LOWRANK] = static_cast<float>(low);
+        for (int i = 0; i < 4; ++i) a.summary[ADA_SUM_N_FP32 + i] = (prec_slot(p) == i) ? 1.f : 0.f;
+        a.summary[ADA_SUM_N_TOTAL] = 1.f;
+    }
+    __syncthreads();
+    for (int64_t i = tid; i < a.BH; i += kThreads) {
+        a.decisions[i * 2 + 0] = s_dec[0];
+        a.decisions[i * 2 + 1] = s_dec[1];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// _adaattn_cuda helper ops (bindings.cpp:101-135) on the device.
+// ---------------------------------------------------------------------------
+struct EntropyArgs {
+    const void* w;
+    int dtype;
+    int64_t rows, len;        // rows of length `len` (contiguous)
+    int64_t group;            // >0: average `group` consecutive row entropies, then exp
+    float* out;
+};
+
+// One warp per row: -sum w * log(w + 1e-10), each op rounded to the dtype.
+__global__ void entropy_rows_kernel(EntropyArgs a) {
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= a.rows) return;
+    const int64_t base = warp * a.len;
+    float acc = 0.f;
+    for (int64_t i = lane; i < a.len; i += 32) {
+        const float w = load_as_f32(a.w, base + i, a.dtype);
+        const float t = round_to(logf(round_to(w + 1e-10f, a.dtype)), a.dtype);
+        acc += round_to(w * t, a.dtype);
+    }
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) a.out[warp] = -round_to(acc, a.dtype);
+}
+
+// exp(mean over `group` consecutive rows of the row entropy): one warp per
+// group walks its rows, so no intermediate buffer is needed.
+__global__ void effective_rank_kernel(const void* w, int dtype, int64_t groups, int64_t group,
+                                      int64_t len, float* out) {
+    const int64_t g = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (g >= groups) return;
+    float total = 0.f;
+    for (int64_t row = 0; row < group; ++row) {
+        const int64_t base = (g * group + row) * len;
+        float acc = 0.f;
+        for (int64_t i = lane; i < len; i += 32) {
+            const float x = load_as_f32(w, base + i, dtype);
+            const float t = round_to(logf(round_to(x + 1e-10f, dtype)), dtype);
+            acc += round_to(x * t, dtype);
+        }
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        total += -round_to(acc, dtype);
+    }
+    if (lane == 0) out[g] = round_to(expf(round_to(total / static_cast<float>(group), dtype)), dtype);
+}
+
+__global__ void target_ranks_kernel(const float* eff, int64_t n, int64_t min_rank, int64_t max_rank,
+                                    double thr, int64_t* out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float e = eff[i];
+    if (static_cast<double>(e) < thr) {
+        float v = e * 1.5f;
+        v = fminf(fmaxf(v, static_cast<float>(min_rank)), static_cast<float>(max_rank));
+        out[i] = static_cast<int64_t>(v);
+    } else {
+        out[i] = max_rank;
+    }
+}
+
+// Waits on a barrier nothing signals; the bounded wait gives up and records
+// ADA_ERR_TIMEOUT, after which the kernel returns normally.
+__global__ void bounded_wait_kernel(uint64_t timeout_ns, unsigned int* status) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, &abort_flag, timeout_ns, status);
+    __syncthreads();
+}
+
+}  // namespace
+
+int launch_analyze(const AnalyzeLaunch& L, cudaStream_t stream) {
+    StatsArgs a{};
+    a.q = L.q;
+    a.k = L.k;
+    a.dtype = L.dtype;
+    a.B = L.B;
+    a.H = L.H;
+    a.Nq = L.Nq;
+    a.Nk = L.Nk;
+    a.D = L.D;
+    for (int i = 0; i < 4; ++i) {
+        a.qs[i] = L.qs[i];
+        a.ks[i] = L.ks[i];
+    }
+    a.scale = L.scale;
+    a.eps = L.eps;
+    a.S = L.S;
+    a.stride = L.stride;
+    a.log_s = static_cast<float>(L.log_s);
+    a.head_stats = L.head_stats;
+    a.head_sum = L.head_sum;
+    const size_t smem = static_cast<size_t>(2 * kSample * (L.D + 1)) * sizeof(float);
+    if (smem > 48 * 1024) {
+        if (cudaFuncSetAttribute(analyze_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)) != cudaSuccess)
+            return ADA_ERR_LAUNCH;
+    }
+    analyze_stats_kernel<<<static_cast<unsigned>(L.B * L.H), kThreads, smem, stream>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return ADA_ERR_LAUNCH;
+
+    DecideArgs d{};
+    d.head_stats = L.head_stats;
+    d.head_sum = L.head_sum;
+    d.decisions = L.decisions;
+    d.summary = L.summary;
+    d.BH = L.B * L.H;
+    d.S = L.S;
+    d.dtype = L.dtype;
+    d.min_n = L.Nq < L.Nk ? L.Nq : L.Nk;
+    d.rank_threshold = L.rank_threshold;
+    d.enable_rank = L.enable_rank;
+    d.enable_prec = L.enable_prec;
+    d.default_prec = L.default_prec;
+    d.allow_fp8 = L.allow_fp8;
+    d.granularity = L.granularity;
+    decide_kernel<<<1, kThreads, 0, stream>>>(d);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+int launch_entropy_rows(const void* w, int dtype, int64_t rows, int64_t len, float* out,
+                        cudaStream_t stream) {
+    EntropyArgs a{w, dtype, rows, len, 0, out};
+    const int threads = 256;
+    const int64_t blocks = (rows * 32 + threads - 1) / threads;
+    if (blocks > 0) entropy_rows_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+int launch_effective_rank(const void* w, int dtype, int64_t groups, int64_t group, int64_t len,
+                          float* out, cudaStream_t stream) {
+    const int threads = 256;
+    const int64_t blocks = (groups * 32 + threads - 1) / threads;
+    if (blocks > 0)
+        effective_rank_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(w, dtype, groups,
+                                                                                    group, len, out);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+int launch_target_ranks(const float* eff, int64_t n, int64_t min_rank, int64_t max_rank, double thr,
+                        int64_t* out, cudaStream_t stream) {
+    const int threads = 256;
+    const int64_t blocks = (n + threads - 1) / threads;
+    if (blocks > 0)
+        target_ranks_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+            eff, n, min_rank, max_rank, thr, out);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+int launch_bounded_wait(uint64_t timeout_ns, unsigned int* status, cudaStream_t stream) {
+    bounded_wait_kernel<<<1, 32, 0, stream>>>(timeout_ns, status);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+}  // namespace ada

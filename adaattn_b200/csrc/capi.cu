@@ -1,0 +1,713 @@
+// The C ABI (include/adaattn_b200.h): argument checking, the per-call launch
+// plan (which kernels serve which heads, workspace carving, TMA descriptors)
+// and the device status word. No entry point here allocates device memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "ada_common.cuh"
+#include "ada_internal.h"
+
+namespace ada {
+namespace {
+
+__device__ unsigned int g_ada_status = 0;
+
+thread_local char g_last_error[512] = {0};
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+unsigned int* g_status_ptr[kMaxDevices] = {nullptr};
+int g_cc_major[kMaxDevices] = {0};
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int current_device(int* dev) {
+    if (cudaGetDevice(dev) != cudaSuccess) return fail(ADA_ERR_DEVICE, "cudaGetDevice failed");
+    if (*dev < 0 || *dev >= kMaxDevices) return fail(ADA_ERR_DEVICE, "device index %d out of range", *dev);
+    return ADA_OK;
+}
+
+// Per-device setup, done once with that device current: check for sm_100 and
+// resolve the device address of the status word.
+int device_setup(unsigned int** status) {
+    int dev;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_cc_major[dev] == 0) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess)
+            return fail(ADA_ERR_DEVICE, "cudaGetDeviceProperties failed");
+        g_cc_major[dev] = prop.major;
+    }
+    if (g_cc_major[dev] != 10)
+        return fail(ADA_ERR_DEVICE, "device %d is sm_%d*, this library is built for sm_100a", dev,
+                    g_cc_major[dev]);
+    if (g_status_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_ada_status);
+        if (e != cudaSuccess) return fail(ADA_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_status_ptr[dev] = static_cast<unsigned int*>(p);
+    }
+    *status = g_status_ptr[dev];
+    return ADA_OK;
+}
+
+int encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_encode == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || p == nullptr)
+            return fail(ADA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    *fn = g_encode;
+    return ADA_OK;
+}
+
+uint64_t wait_timeout_ns() {
+    static uint64_t v = [] {
+        const char* s = getenv("ADA_WAIT_TIMEOUT_MS");
+        long ms = s ? atol(s) : 0;
+        if (ms <= 0) ms = 4000;
+        return static_cast<uint64_t>(ms) * 1000000ull;
+    }();
+    return v;
+}
+
+int elt_bytes(int dtype) {
+    switch (dtype) {
+        case ADA_F32: return 4;
+        case ADA_F16: return 2;
+        case ADA_BF16: return 2;
+        case ADA_E4M3: return 1;
+        case ADA_BOOL: return 1;
+        case ADA_I32: return 4;
+        case ADA_I64: return 8;
+        default: return 0;
+    }
+}
+
+bool is_float(int dtype) { return dtype == ADA_F32 || dtype == ADA_F16 || dtype == ADA_BF16; }
+
+int check_attn_tensor(const AdaTensor* t, const char* name) {
+    if (t == nullptr || t->data == nullptr) return fail(ADA_ERR_INVALID, "%s is null", name);
+    if (t->ndim != 4) return fail(ADA_ERR_SHAPE, "%s must be 4-D [B,H,N,D], got %d-D", name, t->ndim);
+    if (!is_float(t->dtype)) return fail(ADA_ERR_DTYPE, "%s dtype %d unsupported", name, t->dtype);
+    for (int i = 0; i < 4; ++i)
+        if (t->shape[i] < 0) return fail(ADA_ERR_SHAPE, "%s has a negative extent", name);
+    return ADA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// TMA-readable in place: innermost stride 1, other strides multiples of 16
+// bytes, base 16-byte aligned.
+bool tma_ok(const AdaTensor* t) {
+    const int eb = elt_bytes(t->dtype);
+    if (t->stride[3] != 1 && t->shape[3] > 1) return false;
+    if (!aligned16(t->data)) return false;
+    for (int i = 0; i < 3; ++i) {
+        if (t->shape[i] <= 1) continue;
+        if (t->stride[i] <= 0 || ((t->stride[i] * eb) % 16) != 0) return false;
+    }
+    return true;
+}
+
+// 4-D map over [B, H, N, width] (dims innermost first: width, N, H, B) with a
+// 128-row x 128-byte box and 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int eb, int64_t width, int64_t n,
+             int64_t h, int64_t b, int64_t s_n, int64_t s_h, int64_t s_b) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int rc = encoder(&enc);
+    if (rc) return rc;
+    auto fix = [&](int64_t s, int64_t ext, int64_t fallback) {
+        return (ext <= 1 || s <= 0) ? fallback : s;
+    };
+    const int64_t rowb = s_n * eb;
+    const int64_t fb = ((n * rowb + 15) / 16) * 16;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(n > 0 ? n : 1),
+                          static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(b)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(fix(rowb, n, 128)),
+                             static_cast<cuuint64_t>(fix(s_h * eb, h, fb)),
+                             static_cast<cuuint64_t>(fix(s_b * eb, b, fb * (h > 0 ? h : 1)))};
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / eb), 128, 1, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ADA_ERR_LAYOUT, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return ADA_OK;
+}
+
+CUtensorMapDataType tma_dtype(int dtype) {
+    switch (dtype) {
+        case ADA_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        case ADA_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        default: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    }
+}
+
+constexpr uint32_t bit(int p) { return 1u << p; }
+
+// ---------------------------------------------------------------------------
+// The forward plan: derived only from shapes, dtypes, flags and the set of
+// decisions that can occur, so the workspace query and the call agree.
+// ---------------------------------------------------------------------------
+struct Plan {
+    int in_dtype;
+    int64_t B, H, Nq, Nk, D, r;
+    uint32_t possible;
+    bool low_possible, dense_possible;
+    int fp8_mode;
+    uint32_t tc16_mask, f16_mask, fp8_mask, fp32_mask;
+    bool direct_ok;
+    int dqk_dense, dqk_low, dv_pad;
+    int64_t ld16_qk, ld16_v;
+    bool need16, need32, need8;
+    int64_t nt_q, nt_k;
+    size_t off16q, off16k, off16v, off32q, off32k, off8q, off8k, off8v;
+    size_t off_amax_q, off_amax_k, off_amax_v, off_sq, off_sk, off_sv;
+    size_t total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int pad_width(int64_t d) { return d <= 64 ? 64 : 128; }
+
+int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const AdaTensor* w_down,
+               const int32_t* decisions, const AdaFwdParams* p, int32_t possible_mask, int32_t low_possible,
+               Plan* P) {
+    int rc;
+    if ((rc = check_attn_tensor(q, "q")) || (rc = check_attn_tensor(k, "k")) || (rc = check_attn_tensor(v, "v")))
+        return rc;
+    if (p == nullptr) return fail(ADA_ERR_INVALID, "params is null");
+    if (q->dtype != k->dtype || q->dtype != v->dtype)
+        return fail(ADA_ERR_DTYPE, "q, k, v must share one dtype");
+    if (q->shape[0] != k->shape[0] || q->shape[0] != v->shape[0] || q->shape[1] != k->shape[1] ||
+        q->shape[1] != v->shape[1])
+        return fail(ADA_ERR_SHAPE, "batch/head extents of q, k, v differ");
+    if (k->shape[2] != v->shape[2]) return fail(ADA_ERR_SHAPE, "k and v sequence lengths differ");
+    if (q->shape[3] != k->shape[3]) return fail(ADA_ERR_SHAPE, "q and k head dims differ");
+    if (v->shape[3] != q->shape[3]) return fail(ADA_ERR_UNSUPPORTED, "value head dim must equal the query head dim");
+    std::memset(P, 0, sizeof(*P));
+    P->in_dtype = q->dtype;
+    P->B = q->shape[0];
+    P->H = q->shape[1];
+    P->Nq = q->shape[2];
+    P->Nk = k->shape[2];
+    P->D = q->shape[3];
+    if (P->D < 1 || P->D > 128) return fail(ADA_ERR_UNSUPPORTED, "head dim %lld outside [1, 128]", (long long)P->D);
+    P->fp8_mode = p->fp8_mode;
+    if (decisions == nullptr) {
+        if (p->static_precision < 0 || p->static_precision > 4)
+            return fail(ADA_ERR_INVALID, "static precision %d", p->static_precision);
+        P->possible = bit(p->static_precision);
+        P->low_possible = p->static_low_rank != 0;
+        P->dense_possible = p->static_low_rank == 0;
+    } else {
+        P->possible = static_cast<uint32_t>(possible_mask) & 0x1Fu;
+        P->low_possible = low_possible != 0;
+        P->dense_possible = true;
+    }
+    if (P->low_possible) {
+        if (w_down == nullptr || w_down->data == nullptr)
+            return fail(ADA_ERR_INVALID, "low-rank heads need rank_proj_down weights");
+        if (w_down->ndim != 2 || w_down->shape[1] != P->D)
+            return fail(ADA_ERR_SHAPE, "w_down must be [r, D]");
+        if (w_down->stride[1] != 1 || w_down->stride[0] != w_down->shape[1])
+            return fail(ADA_ERR_LAYOUT, "w_down must be contiguous");
+        if (!is_float(w_down->dtype)) return fail(ADA_ERR_DTYPE, "w_down dtype");
+        if (w_down->dtype != P->in_dtype)
+            return fail(ADA_ERR_DTYPE, "rank_proj_down dtype must match the inputs' dtype");
+        P->r = w_down->shape[0];
+        if (P->r < 1 || P->r > 128) return fail(ADA_ERR_UNSUPPORTED, "rank %lld outside [1, 128]", (long long)P->r);
+    }
+    P->tc16_mask = bit(ADA_PREC_FP16) | bit(ADA_PREC_AUTO) | bit(ADA_PREC_BF16) |
+                   (P->fp8_mode == 1 ? bit(ADA_PREC_FP8) : 0u);
+    P->f16_mask = bit(ADA_PREC_FP16) | bit(ADA_PREC_AUTO) | (P->fp8_mode == 1 ? bit(ADA_PREC_FP8) : 0u);
+    P->fp8_mask = P->fp8_mode == 1 ? 0u : bit(ADA_PREC_FP8);
+    P->fp32_mask = bit(ADA_PREC_FP32);
+    P->direct_ok = (P->in_dtype == ADA_F16 || P->in_dtype == ADA_BF16) && (P->D == 64 || P->D == 128) &&
+                   tma_ok(q) && tma_ok(k) && tma_ok(v);
+    P->dqk_dense = pad_width(P->D);
+    P->dv_pad = pad_width(P->D);
+    P->dqk_low = P->low_possible ? pad_width(P->r) : 0;
+    P->ld16_qk = P->dqk_dense > P->dqk_low ? P->dqk_dense : P->dqk_low;
+    P->ld16_v = P->dv_pad;
+    P->need16 = false;
+    for (int pc = 0; pc < 5; ++pc) {
+        if (!((P->possible >> pc) & 1u) || !((P->tc16_mask >> pc) & 1u)) continue;
+        const int cd = ((P->f16_mask >> pc) & 1u) ? ADA_F16 : ADA_BF16;
+        if (P->low_possible || cd != P->in_dtype || !P->direct_ok) P->need16 = true;
+    }
+    P->need32 = ((P->possible & P->fp32_mask) != 0) && P->low_possible;
+    P->need8 = (P->possible & P->fp8_mask) != 0;
+    P->nt_q = (P->Nq + 127) / 128;
+    P->nt_k = (P->Nk + 127) / 128;
+    const int64_t BH = P->B * P->H;
+    size_t off = 0;
+    if (P->need16) {
+        P->off16q = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nq * P->ld16_qk) * 2);
+        P->off16k = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nk * P->ld16_qk) * 2);
+        P->off16v = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nk * P->ld16_v) * 2);
+    }
+    if (P->need32) {
+        P->off32q = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nq * P->r) * 4);
+        P->off32k = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nk * P->r) * 4);
+    }
+    if (P->need8) {
+        P->off8q = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nq * 128));
+        P->off8k = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nk * 128));
+        P->off8v = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nk * 128));
+        P->off_amax_q = off;
+        off = align256(off + static_cast<size_t>(BH * P->nt_q) * 4);
+        P->off_amax_k = off;
+        off = align256(off + static_cast<size_t>(BH * P->nt_k) * 4);
+        P->off_amax_v = off;
+        off = align256(off + static_cast<size_t>(BH * P->nt_k) * 4);
+        P->off_sq = off;
+        off = align256(off + static_cast<size_t>(BH * P->nt_q) * 4);
+        P->off_sk = off;
+        off = align256(off + static_cast<size_t>(BH * P->nt_k) * 4);
+        P->off_sv = off;
+        off = align256(off + static_cast<size_t>(BH) * 4);
+    }
+    P->total = off;
+    return ADA_OK;
+}
+
+MaskView mask_view(const AdaTensor* m) {
+    MaskView mv{};
+    if (m == nullptr || m->data == nullptr) return mv;
+    mv.data = m->data;
+    mv.dtype = m->dtype;
+    for (int i = 0; i < 4; ++i) mv.s[i] = m->shape[i] == 1 ? 0 : m->stride[i];
+    return mv;
+}
+
+int check_mask(const AdaTensor* m, const Plan& P) {
+    if (m == nullptr || m->data == nullptr) return ADA_OK;
+    if (m->ndim != 4) return fail(ADA_ERR_SHAPE, "mask must be a 4-D [B,H,Nq,Nk] view");
+    if (m->dtype != ADA_BOOL && !is_float(m->dtype)) return fail(ADA_ERR_DTYPE, "mask dtype");
+    const int64_t want[4] = {P.B, P.H, P.Nq, P.Nk};
+    for (int i = 0; i < 4; ++i)
+        if (m->shape[i] != want[i] && m->shape[i] != 1)
+            return fail(ADA_ERR_SHAPE, "mask extent %d is %lld, expected %lld or 1", i, (long long)m->shape[i],
+                        (long long)want[i]);
+    return ADA_OK;
+}
+
+bool out_vec_ok(const AdaTensor* o) {
+    const int eb = elt_bytes(o->dtype);
+    if (o->stride[3] != 1 || !aligned16(o->data)) return false;
+    for (int i = 0; i < 3; ++i)
+        if (((o->stride[i] * eb) % 16) != 0) return false;
+    return true;
+}
+
+void copy_strides(int64_t* dst, const AdaTensor* t) {
+    for (int i = 0; i < 4; ++i) dst[i] = t->stride[i];
+}
+
+}  // namespace
+}  // namespace ada
+
+using namespace ada;
+
+extern "C" {
+
+int ada_abi_version(void) { return ADA_ABI_VERSION; }
+
+int ada_get_last_error(char* buf, size_t len) {
+    if (buf == nullptr || len == 0) return ADA_ERR_INVALID;
+    std::strncpy(buf, g_last_error, len - 1);
+    buf[len - 1] = '\0';
+    return ADA_OK;
+}
+
+int ada_poll_device_status(void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned int word = 0;
+    if (cudaMemcpyAsync(&word, st, sizeof(word), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return fail(ADA_ERR_CUDA, "reading the status word failed");
+    if (cudaMemsetAsync(st, 0, sizeof(unsigned int), s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+        return fail(ADA_ERR_CUDA, "clearing the status word failed");
+    if (word == 0) return ADA_OK;
+    for (int i = 0; i < 32; ++i)
+        if (word & (1u << i)) return fail(-(i + 1), "device reported error code %d", -(i + 1));
+    return ADA_OK;
+}
+
+size_t ada_analyze_workspace_bytes(int64_t batch, int64_t heads) {
+    return align256(static_cast<size_t>(batch > 0 ? batch : 0) * static_cast<size_t>(heads > 0 ? heads : 0) *
+                    sizeof(float));
+}
+
+int ada_analyze(const AdaTensor* q, const AdaTensor* k, const AdaAnalyzeParams* params, int32_t* decisions,
+                float* head_stats, float* summary, void* workspace, size_t workspace_bytes, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if ((rc = check_attn_tensor(q, "q")) || (rc = check_attn_tensor(k, "k"))) return rc;
+    if (params == nullptr || decisions == nullptr || head_stats == nullptr || summary == nullptr)
+        return fail(ADA_ERR_INVALID, "null argument");
+    if (q->dtype != k->dtype) return fail(ADA_ERR_DTYPE, "q and k dtypes differ");
+    if (q->shape[0] != k->shape[0] || q->shape[1] != k->shape[1] || q->shape[3] != k->shape[3])
+        return fail(ADA_ERR_SHAPE, "q and k shapes disagree");
+    const int64_t B = q->shape[0], H = q->shape[1], Nq = q->shape[2], Nk = k->shape[2], D = q->shape[3];
+    if (D < 1 || D > 256) return fail(ADA_ERR_UNSUPPORTED, "analyzer head dim %lld outside [1, 256]", (long long)D);
+    if (Nq < 1 || Nk < 1) return fail(ADA_ERR_SHAPE, "empty sequence: the sample size would be 0");
+    const int stride = params->sample_stride > 1 ? params->sample_stride : 1;
+    const int64_t n_min = Nq < Nk ? Nq : Nk;
+    int64_t S = (n_min + stride - 1) / stride;
+    if (S > 64) S = 64;
+    if (B * H == 0) return ADA_OK;
+    if (workspace_bytes < ada_analyze_workspace_bytes(B, H) || workspace == nullptr)
+        return fail(ADA_ERR_WORKSPACE, "analyzer workspace too small");
+    if (params->default_precision < 0 || params->default_precision > 4)
+        return fail(ADA_ERR_INVALID, "default precision %d", params->default_precision);
+    AnalyzeLaunch L{};
+    L.q = q->data;
+    L.k = k->data;
+    L.dtype = q->dtype;
+    L.B = B;
+    L.H = H;
+    L.Nq = Nq;
+    L.Nk = Nk;
+    L.D = D;
+    copy_strides(L.qs, q);
+    copy_strides(L.ks, k);
+    L.scale = params->scale;
+    L.eps = params->eps;
+    L.log_s = std::log(static_cast<double>(S));
+    L.S = static_cast<int>(S);
+    L.stride = stride;
+    L.head_stats = head_stats;
+    L.head_sum = static_cast<float*>(workspace);
+    L.decisions = decisions;
+    L.summary = summary;
+    L.rank_threshold = params->rank_threshold;
+    L.enable_rank = params->enable_adaptive_rank;
+    L.enable_prec = params->enable_adaptive_precision;
+    L.default_prec = params->default_precision;
+    L.allow_fp8 = params->allow_fp8;
+    L.granularity = params->granularity;
+    rc = launch_analyze(L, static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "analyzer launch failed: %s", cudaGetErrorString(cudaGetLastError())) : ADA_OK;
+}
+
+size_t ada_attn_fwd_workspace_bytes(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v,
+                                    const AdaTensor* w_down, const int32_t* decisions, const AdaFwdParams* params,
+                                    int32_t possible_precisions_mask, int32_t low_rank_possible) {
+    Plan P;
+    if (build_plan(q, k, v, w_down, decisions, params, possible_precisions_mask, low_rank_possible, &P)) return 0;
+    return P.total;
+}
+
+int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const AdaTensor* w_down,
+                 const AdaTensor* mask, const int32_t* decisions, const AdaFwdParams* params,
+                 int32_t possible_precisions_mask, int32_t low_rank_possible, AdaTensor* out, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    Plan P;
+    if ((rc = build_plan(q, k, v, w_down, decisions, params, possible_precisions_mask, low_rank_possible, &P)))
+        return rc;
+    if ((rc = check_attn_tensor(out, "out"))) return rc;
+    if (out->dtype != P.in_dtype) return fail(ADA_ERR_DTYPE, "out dtype must match the inputs'");
+    if (out->shape[0] != P.B || out->shape[1] != P.H || out->shape[2] != P.Nq || out->shape[3] != P.D)
+        return fail(ADA_ERR_SHAPE, "out must be [B,H,Nq,D]");
+    if ((rc = check_mask(mask, P))) return rc;
+    if (P.total > 0 && (workspace == nullptr || workspace_bytes < P.total))
+        return fail(ADA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", P.total, workspace_bytes);
+    if (P.B * P.H == 0 || P.Nq == 0) return ADA_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (P.Nk == 0) {
+        // softmax over no keys, then an empty product: the reference returns zeros.
+        return fail(ADA_ERR_SHAPE, "empty key sequence");
+    }
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const DecisionSrc dsrc{decisions, params->static_precision, params->static_low_rank};
+    const MaskView mv = mask_view(mask);
+
+    // ---- operand preparation -------------------------------------------
+    PrepLaunch pl{};
+    pl.dec = dsrc;
+    pl.q = q->data;
+    pl.k = k->data;
+    pl.v = v->data;
+    pl.in_dtype = P.in_dtype;
+    pl.B = P.B;
+    pl.H = P.H;
+    pl.Nq = P.Nq;
+    pl.Nk = P.Nk;
+    pl.D = P.D;
+    copy_strides(pl.qs, q);
+    copy_strides(pl.ks, k);
+    copy_strides(pl.vs, v);
+    pl.w_down = P.low_possible ? w_down->data : nullptr;
+    pl.w_dtype = P.low_possible ? w_down->dtype : ADA_F32;
+    pl.r = P.r;
+    pl.tc16_mask = P.tc16_mask;
+    pl.f16_mask = P.f16_mask;
+    pl.direct_ok = P.direct_ok ? 1 : 0;
+    pl.ld16_qk = P.ld16_qk;
+    pl.ld16_v = P.ld16_v;
+    pl.dqk_dense = P.dqk_dense;
+    pl.dqk_low = P.dqk_low;
+    pl.dv_pad = P.dv_pad;
+    pl.fp32_mask = P.fp32_mask;
+    pl.fp8_mask = P.fp8_mask;
+    pl.nt_q = P.nt_q;
+    pl.nt_k = P.nt_k;
+    if (P.need16) {
+        pl.ws16_q = ws + P.off16q;
+        pl.ws16_k = ws + P.off16k;
+        pl.ws16_v = ws + P.off16v;
+        if ((rc = launch_prep16(pl, s))) return fail(rc, "prep16 launch failed");
+    }
+    if (P.need32) {
+        pl.ws32_q = reinterpret_cast<float*>(ws + P.off32q);
+        pl.ws32_k = reinterpret_cast<float*>(ws + P.off32k);
+        if ((rc = launch_prep32(pl, s))) return fail(rc, "prep32 launch failed");
+    }
+    if (P.need8) {
+        pl.ws8_q = ws + P.off8q;
+        pl.ws8_k = ws + P.off8k;
+        pl.ws8_v = ws + P.off8v;
+        pl.amax_q = reinterpret_cast<float*>(ws + P.off_amax_q);
+        pl.amax_k = reinterpret_cast<float*>(ws + P.off_amax_k);
+        pl.amax_v = reinterpret_cast<float*>(ws + P.off_amax_v);
+        pl.scale_q = reinterpret_cast<float*>(ws + P.off_sq);
+        pl.scale_k = reinterpret_cast<float*>(ws + P.off_sk);
+        pl.scale_v = reinterpret_cast<float*>(ws + P.off_sv);
+        if ((rc = launch_prep8(pl, s))) return fail(rc, "prep8 launch failed");
+    }
+
+    // ---- tensor-core launches ---------------------------------------------
+    const float log2e = 1.4426950408889634f;
+    auto base_tc = [&](TcLaunch& L) {
+        std::memset(&L, 0, sizeof(L));
+        L.B = P.B;
+        L.H = P.H;
+        L.Nq = P.Nq;
+        L.Nk = P.Nk;
+        L.dv_out = static_cast<int>(P.D);
+        L.out = out->data;
+        L.out_dtype = out->dtype;
+        copy_strides(L.os, out);
+        L.out_vec = out_vec_ok(out) ? 1 : 0;
+        L.scale_log2 = params->scale * log2e;
+        L.causal = params->causal;
+        L.mask = mv;
+        L.status = st;
+        L.timeout_ns = wait_timeout_ns();
+        L.nt_q = P.nt_q;
+        L.nt_k = P.nt_k;
+    };
+    for (int cdi = 0; cdi < 2; ++cdi) {
+        const int cd = cdi == 0 ? ADA_F16 : ADA_BF16;
+        const uint32_t pm = P.possible & P.tc16_mask & (cd == ADA_F16 ? P.f16_mask : ~P.f16_mask);
+        if (pm == 0) continue;
+        const CUtensorMapDataType dt = tma_dtype(cd);
+        for (int low = 0; low < 2; ++low) {
+            if (low ? !P.low_possible : !P.dense_possible) continue;
+            TcLaunch L;
+            base_tc(L);
+            L.elt = cd == ADA_BF16 ? 1 : 0;
+            L.round_dtype = cd;
+            L.sel = HeadSelect{decisions, pm, low};
+            const bool direct = !low && cd == P.in_dtype && P.direct_ok;
+            if (direct) {
+                L.dqk = static_cast<int>(P.D);
+                L.dv = static_cast<int>(P.D);
+                if ((rc = make_map(&L.tq, q->data, dt, 2, P.D, P.Nq, P.H, P.B, q->stride[2], q->stride[1], q->stride[0])) ||
+                    (rc = make_map(&L.tk, k->data, dt, 2, P.D, P.Nk, P.H, P.B, k->stride[2], k->stride[1], k->stride[0])) ||
+                    (rc = make_map(&L.tv, v->data, dt, 2, P.D, P.Nk, P.H, P.B, v->stride[2], v->stride[1], v->stride[0])))
+                    return rc;
+            } else {
+                L.dqk = low ? P.dqk_low : P.dqk_dense;
+                L.dv = P.dv_pad;
+                const int64_t l = P.ld16_qk, lv = P.ld16_v;
+                if ((rc = make_map(&L.tq, ws + P.off16q, dt, 2, L.dqk, P.Nq, P.H, P.B, l, P.Nq * l, P.H * P.Nq * l)) ||
+                    (rc = make_map(&L.tk, ws + P.off16k, dt, 2, L.dqk, P.Nk, P.H, P.B, l, P.Nk * l, P.H * P.Nk * l)) ||
+                    (rc = make_map(&L.tv, ws + P.off16v, dt, 2, L.dv, P.Nk, P.H, P.B, lv, P.Nk * lv, P.H * P.Nk * lv)))
+                    return rc;
+            }
+            if ((rc = launch_fmha_tc(L, s))) return fail(rc, "tensor-core attention launch failed (%d,%d)", L.dqk, L.dv);
+        }
+    }
+    if (P.need8) {
+        for (int low = 0; low < 2; ++low) {
+            if (low ? !P.low_possible : !P.dense_possible) continue;
+            TcLaunch L;
+            base_tc(L);
+            L.elt = 2;
+            L.round_dtype = ADA_F16;  // the reference's FP8 mode yields fp16 results
+            L.sel = HeadSelect{decisions, P.fp8_mask, low};
+            L.dqk = 128;
+            L.dv = 128;
+            L.q_scale = reinterpret_cast<float*>(ws + P.off_sq);
+            L.k_scale = reinterpret_cast<float*>(ws + P.off_sk);
+            L.v_scale = reinterpret_cast<float*>(ws + P.off_sv);
+            const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+            if ((rc = make_map(&L.tq, ws + P.off8q, dt, 1, 128, P.Nq, P.H, P.B, 128, P.Nq * 128, P.H * P.Nq * 128)) ||
+                (rc = make_map(&L.tk, ws + P.off8k, dt, 1, 128, P.Nk, P.H, P.B, 128, P.Nk * 128, P.H * P.Nk * 128)) ||
+                (rc = make_map(&L.tv, ws + P.off8v, dt, 1, 128, P.Nk, P.H, P.B, 128, P.Nk * 128, P.H * P.Nk * 128)))
+                return rc;
+            if ((rc = launch_fmha_tc(L, s))) return fail(rc, "E4M3 attention launch failed");
+        }
+    }
+    // ---- fp32 heads on the CUDA cores ---------------------------------------
+    if (P.possible & P.fp32_mask) {
+        for (int low = 0; low < 2; ++low) {
+            if (low ? !P.low_possible : !P.dense_possible) continue;
+            SimtLaunch L{};
+            L.B = P.B;
+            L.H = P.H;
+            L.Nq = P.Nq;
+            L.Nk = P.Nk;
+            L.v = v->data;
+            L.v_dtype = P.in_dtype;
+            copy_strides(L.vs, v);
+            L.dv = static_cast<int>(P.D);
+            L.out = out->data;
+            L.out_dtype = out->dtype;
+            copy_strides(L.os, out);
+            L.scale = params->scale;
+            L.causal = params->causal;
+            L.mask = mv;
+            L.sel = HeadSelect{decisions, P.fp32_mask, low};
+            if (low) {
+                L.q = ws + P.off32q;
+                L.k = ws + P.off32k;
+                L.q_dtype = L.k_dtype = ADA_F32;
+                const int64_t r = P.r;
+                const int64_t qs[4] = {P.H * P.Nq * r, P.Nq * r, r, 1};
+                const int64_t ks[4] = {P.H * P.Nk * r, P.Nk * r, r, 1};
+                std::memcpy(L.qs, qs, sizeof(qs));
+                std::memcpy(L.ks, ks, sizeof(ks));
+                L.dqk = static_cast<int>(r);
+            } else {
+                L.q = q->data;
+                L.k = k->data;
+                L.q_dtype = L.k_dtype = P.in_dtype;
+                copy_strides(L.qs, q);
+                copy_strides(L.ks, k);
+                L.dqk = static_cast<int>(P.D);
+            }
+            if ((rc = launch_fmha_simt(L, s))) return fail(rc, "fp32 attention launch failed");
+        }
+    }
+    return ADA_OK;
+}
+
+int ada_flash_attention_forward(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, float scale,
+                                int32_t causal, AdaTensor* out, void* stream) {
+    // [B, N, H, D] views -> [B, H, N, D] by swapping the middle extents.
+    auto perm = [](const AdaTensor* t) {
+        AdaTensor r = *t;
+        if (t->ndim == 4) {
+            r.shape[1] = t->shape[2];
+            r.shape[2] = t->shape[1];
+            r.stride[1] = t->stride[2];
+            r.stride[2] = t->stride[1];
+        }
+        return r;
+    };
+    int rc;
+    if ((rc = check_attn_tensor(q, "q")) || (rc = check_attn_tensor(out, "out"))) return rc;
+    AdaTensor qp = perm(q), kp = perm(k), vp = perm(v), op = perm(out);
+    AdaFwdParams p{};
+    p.scale = scale > 0.f ? scale : 1.f / std::sqrt(static_cast<float>(q->shape[3]));
+    p.causal = causal;
+    p.static_precision = q->dtype == ADA_F16 ? ADA_PREC_FP16 : (q->dtype == ADA_BF16 ? ADA_PREC_BF16 : ADA_PREC_FP32);
+    p.static_low_rank = 0;
+    return ada_attn_fwd(&qp, &kp, &vp, nullptr, nullptr, nullptr, &p, 0, 0, &op, nullptr, 0, stream);
+}
+
+int ada_compute_entropy(const AdaTensor* w, float* entropy_out, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if (w == nullptr || w->data == nullptr || entropy_out == nullptr) return fail(ADA_ERR_INVALID, "null argument");
+    if (w->ndim < 1 || w->ndim > 4 || !is_float(w->dtype)) return fail(ADA_ERR_SHAPE, "weights must be 1-4-D float");
+    int64_t expect = 1, rows = 1;
+    for (int i = w->ndim - 1; i >= 0; --i) {
+        if (w->stride[i] != expect && w->shape[i] > 1) return fail(ADA_ERR_LAYOUT, "weights must be contiguous");
+        expect *= w->shape[i];
+        if (i < w->ndim - 1) rows *= w->shape[i];
+    }
+    rc = launch_entropy_rows(w->data, w->dtype, rows, w->shape[w->ndim - 1], entropy_out,
+                             static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "entropy launch failed") : ADA_OK;
+}
+
+int ada_estimate_effective_rank(const AdaTensor* w, float* rank_out, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if (w == nullptr || w->data == nullptr || rank_out == nullptr) return fail(ADA_ERR_INVALID, "null argument");
+    if (w->ndim < 2 || w->ndim > 4 || !is_float(w->dtype)) return fail(ADA_ERR_SHAPE, "weights must be 2-4-D float");
+    int64_t expect = 1, groups = 1;
+    for (int i = w->ndim - 1; i >= 0; --i) {
+        if (w->stride[i] != expect && w->shape[i] > 1) return fail(ADA_ERR_LAYOUT, "weights must be contiguous");
+        expect *= w->shape[i];
+        if (i < w->ndim - 2) groups *= w->shape[i];
+    }
+    rc = launch_effective_rank(w->data, w->dtype, groups, w->shape[w->ndim - 2], w->shape[w->ndim - 1], rank_out,
+                               static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "effective-rank launch failed") : ADA_OK;
+}
+
+int ada_determine_target_ranks(const float* eff, int64_t n, int64_t min_rank, int64_t max_rank, double threshold,
+                               int64_t* ranks_out, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if ((eff == nullptr || ranks_out == nullptr) && n > 0) return fail(ADA_ERR_INVALID, "null argument");
+    rc = launch_target_ranks(eff, n, min_rank, max_rank, threshold, ranks_out, static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "target-rank launch failed") : ADA_OK;
+}
+
+int ada_debug_bounded_wait(uint64_t timeout_ns, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    rc = launch_bounded_wait(timeout_ns, st, static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "bounded-wait launch failed") : ADA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,315 @@
+// Operand preparation for the attention kernels, driven by the per-head
+// decision table on the device (no host round trip):
+//   prep16  heads computed by the 16-bit tensor-core kernels that cannot be
+//           read in place: cast to the compute dtype (adaattn.py:303-305,
+//           :361-363), or project q and k through rank_proj_down first
+//           (adaattn.py:357-358, a Linear in the inputs' dtype), and pad the
+//           head dimension with zeros to a whole 128-byte row.
+//   prep32  FP32 low-rank heads: q_low / k_low in fp32 for the SIMT kernel.
+//   prep8   FP8 heads in E4M3 mode: per-tile amax, then tile-scaled E4M3
+//           values (Q, K: one scale per 128-row tile; V: one per head).
+#include "ada_common.cuh"
+#include "ada_internal.h"
+
+namespace ada {
+namespace {
+
+constexpr int kRows = 64;
+constexpr int kThreads = 256;
+
+// x[64 rows] . W^T -> y[64 rows, r] with W^T staged in shared memory as fp32.
+// Each thread owns one row and r/4 output columns (col = c4 + 4*i). The
+// result is rounded to the inputs' dtype, as the reference's Linear returns
+// a tensor of that dtype.
+struct ProjSmem {
+    float* w_t;  // [D][r]
+    float* x;    // [kRows][D + 1]
+};
+
+__device__ void stage_weight(const PrepLaunch& L, float* w_t) {
+    const int D = static_cast<int>(L.D), r = static_cast<int>(L.r);
+    for (int i = threadIdx.x; i < D * r; i += kThreads) {
+        const int rr = i / D, d = i - rr * D;
+        w_t[d * r + rr] = load_as_f32(L.w_down, i, L.w_dtype);
+    }
+}
+
+__device__ void stage_rows(const void* x, int dtype, const int64_t* st, int64_t b, int64_t h,
+                           int64_t row0, int64_t nrows, int D, float* sx) {
+    const int64_t base = b * st[0] + h * st[1];
+    for (int i = threadIdx.x; i < kRows * D; i += kThreads) {
+        const int rr = i / D, d = i - rr * D;
+        const int64_t row = row0 + rr;
+        sx[rr * (D + 1) + d] = row < nrows ? load_as_f32(x, base + row * st[2] + d * st[3], dtype) : 0.f;
+    }
+}
+
+// y[c] for this thread's row; cols c = c4 + 4*i, i < 32 (r <= 128).
+__device__ void project_row(const float* sx, const float* w_t, int D, int r, int row, int c4,
+                            float (&y)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) y[i] = 0.f;
+    const float* xr = sx + row * (D + 1);
+    for (int d = 0; d < D; ++d) {
+        const float xv = xr[d];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int c = c4 + 4 * i;
+            if (c < r) y[i] = fmaf(xv, w_t[d * r + c], y[i]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) prep16_kernel(const __grid_constant__ PrepLaunch L) {
+    extern __shared__ float sm[];
+    const int64_t bh = blockIdx.y;
+    int prec, low;
+    get_decision(L.dec, bh, &prec, &low);
+    if (!((L.tc16_mask >> prec) & 1u)) return;
+    const int cd = ((L.f16_mask >> prec) & 1u) ? ADA_F16 : ADA_BF16;
+    const bool needs = low || cd != L.in_dtype || !L.direct_ok;
+    if (!needs) return;
+    const int64_t b = bh / L.H, h = bh % L.H;
+    const int D = static_cast<int>(L.D);
+    const int r = static_cast<int>(L.r);
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
+    const int dqk_w = low ? L.dqk_low : L.dqk_dense;
+
+    float* w_t = sm;
+    float* sx = sm + (low ? D * r : 0);
+    if (low) stage_weight(L, w_t);
+
+    for (int which = 0; which < 2; ++which) {  // 0: q, 1: k
+        const int64_t nrows = which == 0 ? L.Nq : L.Nk;
+        if (row0 >= nrows) continue;
+        const void* x = which == 0 ? L.q : L.k;
+        const int64_t* st = which == 0 ? L.qs : L.ks;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(which == 0 ? L.ws16_q : L.ws16_k);
+        const int64_t plane = (which == 0 ? L.Nq : L.Nk) * L.ld16_qk;
+        if (low) {
+            __syncthreads();
+            stage_rows(x, L.in_dtype, st, b, h, row0, nrows, D, sx);
+            __syncthreads();
+            const int row = threadIdx.x >> 2, c4 = threadIdx.x & 3;
+            float y[32];
+            project_row(sx, w_t, D, r, row, c4, y);
+            const int64_t grow = row0 + row;
+            if (grow < nrows) {
+                void* out = dst + bh * plane + grow * L.ld16_qk;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int c = c4 + 4 * i;
+                    if (c < dqk_w) store_from_f32(out, c, cd, c < r ? round_to(y[i], L.in_dtype) : 0.f);
+                }
+            }
+        } else {
+            const int64_t base = b * st[0] + h * st[1];
+            for (int i = threadIdx.x; i < kRows * dqk_w; i += kThreads) {
+                const int rr = i / dqk_w, c = i - rr * dqk_w;
+                const int64_t grow = row0 + rr;
+                if (grow >= nrows) continue;
+                const float val = c < D ? load_as_f32(x, base + grow * st[2] + c * st[3], L.in_dtype) : 0.f;
+                store_from_f32(dst + bh * plane + grow * L.ld16_qk, c, cd, val);
+            }
+        }
+    }
+    if (row0 < L.Nk) {
+        const int64_t base = b * L.vs[0] + h * L.vs[1];
+        uint16_t* dst = reinterpret_cast<uint16_t*>(L.ws16_v) + bh * L.Nk * L.ld16_v;
+        for (int i = threadIdx.x; i < kRows * L.dv_pad; i += kThreads) {
+            const int rr = i / L.dv_pad, c = i - rr * L.dv_pad;
+            const int64_t grow = row0 + rr;
+            if (grow >= L.Nk) continue;
+            const float val = c < D ? load_as_f32(L.v, base + grow * L.vs[2] + c * L.vs[3], L.in_dtype) : 0.f;
+            store_from_f32(dst + grow * L.ld16_v, c, cd, val);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) prep32_kernel(const __grid_constant__ PrepLaunch L) {
+    extern __shared__ float sm[];
+    const int64_t bh = blockIdx.y;
+    int prec, low;
+    get_decision(L.dec, bh, &prec, &low);
+    if (!low || !((L.fp32_mask >> prec) & 1u)) return;
+    const int64_t b = bh / L.H, h = bh % L.H;
+    const int D = static_cast<int>(L.D);
+    const int r = static_cast<int>(L.r);
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
+    float* w_t = sm;
+    float* sx = sm + D * r;
+    stage_weight(L, w_t);
+    for (int which = 0; which < 2; ++which) {
+        const int64_t nrows = which == 0 ? L.Nq : L.Nk;
+        if (row0 >= nrows) continue;
+        __syncthreads();
+        stage_rows(which == 0 ? L.q : L.k, L.in_dtype, which == 0 ? L.qs : L.ks, b, h, row0, nrows, D, sx);
+        __syncthreads();
+        const int row = threadIdx.x >> 2, c4 = threadIdx.x & 3;
+        float y[32];
+        project_row(sx, w_t, D, r, row, c4, y);
+        const int64_t grow = row0 + row;
+        if (grow < nrows) {
+            float* out = (which == 0 ? L.ws32_q : L.ws32_k) + (bh * nrows + grow) * r;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int c = c4 + 4 * i;
+                if (c < r) out[c] = round_to(y[i], L.in_dtype);
+            }
+        }
+    }
+}
+
+// ---------------- E4M3 ----------------
+// pass 0: amax of each 128-row tile of Q (or q_low), K (or k_low) and V.
+// pass 1: quantise with scale = amax / 448 (1 when amax is 0); V uses the
+//         largest tile amax of its head.
+__global__ void __launch_bounds__(kThreads) prep8_kernel(const __grid_constant__ PrepLaunch L, int pass) {
+    extern __shared__ float sm[];
+    __shared__ unsigned int s_amax[3];
+    __shared__ float s_scale[3];
+    const int64_t bh = blockIdx.y;
+    int prec, low;
+    get_decision(L.dec, bh, &prec, &low);
+    if (!((L.fp8_mask >> prec) & 1u)) return;
+    const int64_t b = bh / L.H, h = bh % L.H;
+    const int D = static_cast<int>(L.D);
+    const int r = static_cast<int>(L.r);
+    const int64_t tile = blockIdx.x;
+    if (threadIdx.x < 3) s_amax[threadIdx.x] = 0u;
+    float* w_t = sm;
+    float* sx = sm + (low ? D * r : 0);
+    if (low) stage_weight(L, w_t);
+    if (pass == 1 && threadIdx.x == 0) {
+        float sq = 1.f, sk = 1.f, svv = 0.f;
+        if (tile < L.nt_q) {
+            const float a = L.amax_q[bh * L.nt_q + tile];
+            sq = a > 0.f ? a / 448.f : 1.f;
+            L.scale_q[bh * L.nt_q + tile] = sq;
+        }
+        if (tile < L.nt_k) {
+            const float a = L.amax_k[bh * L.nt_k + tile];
+            sk = a > 0.f ? a / 448.f : 1.f;
+            L.scale_k[bh * L.nt_k + tile] = sk;
+        }
+        for (int64_t t = 0; t < L.nt_k; ++t) svv = fmaxf(svv, L.amax_v[bh * L.nt_k + t]);
+        const float sv = svv > 0.f ? svv / 448.f : 1.f;
+        if (tile == 0) L.scale_v[bh] = sv;
+        s_scale[0] = sq;
+        s_scale[1] = sk;
+        s_scale[2] = sv;
+    }
+    __syncthreads();
+    for (int which = 0; which < 3; ++which) {  // q, k, v
+        const int64_t nrows = which == 0 ? L.Nq : L.Nk;
+        const int64_t nt = which == 0 ? L.nt_q : L.nt_k;
+        if (tile >= nt) continue;
+        const void* x = which == 0 ? L.q : (which == 1 ? L.k : L.v);
+        const int64_t* st = which == 0 ? L.qs : (which == 1 ? L.ks : L.vs);
+        uint8_t* dst8 = which == 0 ? L.ws8_q : (which == 1 ? L.ws8_k : L.ws8_v);
+        const bool proj = low && which < 2;
+        const int width = proj ? r : D;
+        float amax = 0.f;
+        for (int half = 0; half < 2; ++half) {
+            const int64_t row0 = tile * 128 + half * kRows;
+            if (row0 >= nrows) break;
+            __syncthreads();
+            if (proj) {
+                stage_rows(x, L.in_dtype, st, b, h, row0, nrows, D, sx);
+                __syncthreads();
+                const int row = threadIdx.x >> 2, c4 = threadIdx.x & 3;
+                float y[32];
+                project_row(sx, w_t, D, r, row, c4, y);
+                const int64_t grow = row0 + row;
+                const bool rok = grow < nrows;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int c = c4 + 4 * i;
+                    const float val = (rok && c < r) ? round_to(y[i], L.in_dtype) : 0.f;
+                    amax = fmaxf(amax, fabsf(val));
+                    if (pass == 1 && rok) {
+                        const float qv = val / s_scale[which];
+                        dst8[(bh * nrows + grow) * 128 + c] =
+                            __nv_cvt_float_to_fp8(qv, __NV_SATFINITE, __NV_E4M3);
+                    }
+                }
+            } else {
+                const int64_t base = b * st[0] + h * st[1];
+                for (int i = threadIdx.x; i < kRows * 128; i += kThreads) {
+                    const int rr = i >> 7, c = i & 127;
+                    const int64_t grow = row0 + rr;
+                    if (grow >= nrows) continue;
+                    const float val = c < width ? load_as_f32(x, base + grow * st[2] + c * st[3], L.in_dtype) : 0.f;
+                    amax = fmaxf(amax, fabsf(val));
+                    if (pass == 1) {
+                        dst8[(bh * nrows + grow) * 128 + c] =
+                            __nv_cvt_float_to_fp8(val / s_scale[which], __NV_SATFINITE, __NV_E4M3);
+                    }
+                }
+            }
+        }
+        if (pass == 0) {
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            if ((threadIdx.x & 31) == 0) atomicMax(&s_amax[which], __float_as_uint(amax));
+        }
+    }
+    if (pass == 0) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            if (tile < L.nt_q) L.amax_q[bh * L.nt_q + tile] = __uint_as_float(s_amax[0]);
+            if (tile < L.nt_k) {
+                L.amax_k[bh * L.nt_k + tile] = __uint_as_float(s_amax[1]);
+                L.amax_v[bh * L.nt_k + tile] = __uint_as_float(s_amax[2]);
+            }
+        }
+    }
+}
+
+size_t proj_smem(const PrepLaunch& L, bool with_weight) {
+    size_t f = static_cast<size_t>(kRows) * (L.D + 1);
+    if (with_weight) f += static_cast<size_t>(L.D) * L.r;
+    return f * sizeof(float);
+}
+
+template <typename K>
+int set_smem(K kern, size_t smem) {
+    if (smem > 48 * 1024)
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+            cudaSuccess)
+            return ADA_ERR_LAUNCH;
+    return ADA_OK;
+}
+
+}  // namespace
+
+int launch_prep16(const PrepLaunch& L, cudaStream_t stream) {
+    const int64_t nt = ((L.Nq > L.Nk ? L.Nq : L.Nk) + kRows - 1) / kRows;
+    if (nt == 0 || L.B * L.H == 0) return ADA_OK;
+    const size_t smem = proj_smem(L, L.w_down != nullptr);
+    if (set_smem(prep16_kernel, smem) != ADA_OK) return ADA_ERR_LAUNCH;
+    prep16_kernel<<<dim3(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H)), kThreads, smem, stream>>>(L);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+int launch_prep32(const PrepLaunch& L, cudaStream_t stream) {
+    const int64_t nt = ((L.Nq > L.Nk ? L.Nq : L.Nk) + kRows - 1) / kRows;
+    if (nt == 0 || L.B * L.H == 0 || L.w_down == nullptr) return ADA_OK;
+    const size_t smem = proj_smem(L, true);
+    if (set_smem(prep32_kernel, smem) != ADA_OK) return ADA_ERR_LAUNCH;
+    prep32_kernel<<<dim3(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H)), kThreads, smem, stream>>>(L);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+int launch_prep8(const PrepLaunch& L, cudaStream_t stream) {
+    const int64_t nt = L.nt_q > L.nt_k ? L.nt_q : L.nt_k;
+    if (nt == 0 || L.B * L.H == 0) return ADA_OK;
+    const size_t smem = proj_smem(L, L.w_down != nullptr);
+    if (set_smem(prep8_kernel, smem) != ADA_OK) return ADA_ERR_LAUNCH;
+    const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H));
+    prep8_kernel<<<grid, kThreads, smem, stream>>>(L, 0);
+    if (cudaGetLastError() != cudaSuccess) return ADA_ERR_LAUNCH;
+    prep8_kernel<<<grid, kThreads, smem, stream>>>(L, 1);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+}  // namespace ada

@@ -1,0 +1,186 @@
+/*
+ * adaattn_b200.h -- C ABI of the B200 (sm_100a) AdaAttn attention-forward path.
+ *
+ * Plain pointers, sizes and POD structs only: no C++ or framework types cross
+ * this boundary. Every entry point returns ADA_OK (0) or a negative ADA_ERR_*
+ * code; ada_get_last_error() gives the message of the calling thread's last
+ * failure. All device work is enqueued on the caller's stream (a cudaStream_t
+ * passed as void*; NULL is the legacy default stream) and nothing synchronises
+ * unless the entry point says so. Device buffers are owned by the caller; an
+ * entry point that needs scratch memory takes a caller-provided workspace
+ * whose size comes from the matching *_workspace_bytes query.
+ *
+ * Reference interfaces replaced (paths inside hkevin01/AdaAttn):
+ *   - the pybind11 module `_adaattn_cuda`, src/adaattn/kernels/bindings.cpp:140-189
+ *     (flash_attention_forward, adaptive_attention_forward, compute_entropy,
+ *     estimate_effective_rank, determine_target_ranks), imported at
+ *     src/adaattn/kernels/__init__.py:39-48 and called at :76-79, :148-151;
+ *   - AdaAttention's analyzer and adaptive core,
+ *     src/adaattn/attention/adaattn.py:228-289 and :462-504, and the flash_attn
+ *     branch it takes on CUDA, src/adaattn/attention/adaattn.py:421-445.
+ */
+#ifndef ADAATTN_B200_H
+#define ADAATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ADA_ABI_VERSION 1
+
+/* ---- status codes ---------------------------------------------------- */
+#define ADA_OK               0
+#define ADA_ERR_INVALID     -1  /* null pointer or parameter out of range   */
+#define ADA_ERR_SHAPE       -2  /* tensor shapes disagree                    */
+#define ADA_ERR_DTYPE       -3  /* unsupported element type                  */
+#define ADA_ERR_DEVICE      -4  /* no sm_100 device / pointer not on device  */
+#define ADA_ERR_LAYOUT      -5  /* stride or alignment the kernels cannot use */
+#define ADA_ERR_LAUNCH      -6  /* kernel launch failed                      */
+#define ADA_ERR_TIMEOUT     -7  /* a device-side wait hit its time limit     */
+#define ADA_ERR_WORKSPACE   -8  /* workspace missing or too small            */
+#define ADA_ERR_UNSUPPORTED -9  /* valid request outside what is built       */
+#define ADA_ERR_CUDA       -10  /* CUDA runtime error                        */
+
+/* ---- element types ---------------------------------------------------- */
+#define ADA_F32   0
+#define ADA_F16   1
+#define ADA_BF16  2
+#define ADA_E4M3  3
+#define ADA_BOOL  4   /* one byte per element, nonzero = keep */
+#define ADA_I32   5
+#define ADA_I64   6
+
+/* ---- precision codes: the reference's _precision_distribution order
+ *      (src/adaattn/attention/adaattn.py:480-485) plus AUTO, which computes
+ *      in fp16 (base.py:107) and is counted in the FP32 slot (.get(p, 0)). */
+#define ADA_PREC_FP32 0
+#define ADA_PREC_FP16 1
+#define ADA_PREC_BF16 2
+#define ADA_PREC_FP8  3
+#define ADA_PREC_AUTO 4
+
+/* A strided view of up to 4 dimensions; strides are in elements. For the
+ * attention entry points q/k/v/out are [B, H, N, D] (any strides with the
+ * last one equal to 1; a [B, N, H, D] buffer is passed by permuting strides).
+ * A mask is [B, H, Nq, Nk] with stride 0 on broadcast dimensions. */
+typedef struct AdaTensor {
+    void*   data;
+    int32_t dtype;
+    int32_t ndim;
+    int64_t shape[4];
+    int64_t stride[4];
+} AdaTensor;
+
+/* Analyzer knobs; defaults in brackets follow adaattn.py:57-79, base.py:203. */
+typedef struct AdaAnalyzeParams {
+    double  rank_threshold;             /* low rank when ne < this [0.95]; compared in double like the reference's Python floats */
+    float   scale;                      /* softmax scale [1/sqrt(D)]           */
+    float   eps;                        /* entropy epsilon [1e-6]              */
+    int32_t enable_adaptive_rank;       /* [1]                                  */
+    int32_t enable_adaptive_precision;  /* [1]                                  */
+    int32_t default_precision;          /* ADA_PREC_* [FP16]                    */
+    int32_t allow_fp8;                  /* [0]                                  */
+    int32_t granularity;                /* 0: one decision per (b,h); 1: one per call (reference) */
+    int32_t sample_stride;              /* 1: first 64 rows (reference); s>1: rows 0, s, 2s, ... */
+    int32_t reserved[2];
+} AdaAnalyzeParams;
+
+/* Outputs of ada_analyze (device buffers):
+ *   decisions  int32 [B*H*2]  {precision code, low_rank flag} per (b,h)
+ *   head_stats f32   [B*H*4]  {normalized entropy, max|score|, max prob, effective rank}
+ *   summary    f32   [ADA_SUMMARY_LEN]  see ADA_SUM_* */
+#define ADA_SUMMARY_LEN 12
+#define ADA_SUM_NE        0
+#define ADA_SUM_MAX_SCORE 1
+#define ADA_SUM_MAX_PROB  2
+#define ADA_SUM_EFF_RANK  3
+#define ADA_SUM_N_LOWRANK 4
+#define ADA_SUM_N_FP32    5   /* counts per precision slot: FP32(+AUTO), FP16, BF16, FP8 */
+#define ADA_SUM_N_FP16    6
+#define ADA_SUM_N_BF16    7
+#define ADA_SUM_N_FP8     8
+#define ADA_SUM_N_TOTAL   9
+
+/* Forward knobs. */
+typedef struct AdaFwdParams {
+    float   scale;          /* softmax scale applied to q.k (both branches use 1/sqrt(D), adaattn.py:144) */
+    int32_t causal;         /* top-left aligned: key j hidden from query i when j > i */
+    int32_t fp8_mode;       /* 0: FP8 heads use tile-scaled E4M3 tensor cores; 1: fp16 arithmetic like base.py:106 */
+    int32_t static_precision; /* used when decisions == NULL */
+    int32_t static_low_rank;  /* used when decisions == NULL */
+    int32_t reserved[3];
+} AdaFwdParams;
+
+int         ada_abi_version(void);
+int         ada_get_last_error(char* buf, size_t len);
+/* Reads and clears the library's device status word on the current device
+ * (synchronises `stream`). Returns ADA_OK or the first ADA_ERR_* a kernel
+ * recorded, e.g. ADA_ERR_TIMEOUT from a bounded wait. */
+int         ada_poll_device_status(void* stream);
+
+/* Per-head statistics and decisions of the analyzer sample.
+ * Replaces AdaAttention._analyze_attention_pattern (adaattn.py:228-289) and
+ * the _adaattn_cuda helpers compute_entropy / estimate_effective_rank /
+ * determine_target_ranks (bindings.cpp:101-135) on the attention path.
+ * No host synchronisation: the decision is written to device memory. */
+size_t      ada_analyze_workspace_bytes(int64_t batch, int64_t heads);
+int         ada_analyze(const AdaTensor* q, const AdaTensor* k,
+                        const AdaAnalyzeParams* params,
+                        int32_t* decisions, float* head_stats, float* summary,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Adaptive attention core on [B,H,N,D]: every (b,h) slice takes the branch
+ * (dense / low rank) and the precision its decision names. Replaces
+ * AdaAttention._adaptive_attention_forward (adaattn.py:462-504) with
+ * _compute_dense_attention (:291-339) and _compute_low_rank_attention
+ * (:341-394), and _adaattn_cuda.adaptive_attention_forward (bindings.cpp:73-96).
+ *   decisions: device int32 [B*H*2] from ada_analyze, or NULL to use
+ *              params->static_precision / static_low_rank for every head.
+ *   w_down:    rank_proj_down.weight [r, D] (adaattn.py:133), or NULL when no
+ *              head can take the low-rank branch.
+ *   mask:      optional [B,H,Nq,Nk] view (bool keeps True; float is added),
+ *              as adaattn.py:320-329.
+ *   out:       [B,H,Nq,Dv] in the inputs' dtype. */
+size_t      ada_attn_fwd_workspace_bytes(const AdaTensor* q, const AdaTensor* k,
+                                         const AdaTensor* v, const AdaTensor* w_down,
+                                         const int32_t* decisions,
+                                         const AdaFwdParams* params,
+                                         int32_t possible_precisions_mask,
+                                         int32_t low_rank_possible);
+int         ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v,
+                         const AdaTensor* w_down, const AdaTensor* mask,
+                         const int32_t* decisions, const AdaFwdParams* params,
+                         int32_t possible_precisions_mask, int32_t low_rank_possible,
+                         AdaTensor* out, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* _adaattn_cuda.flash_attention_forward (bindings.cpp:21-68): q, k, v, out are
+ * [B, N, H, D] fp16/bf16 (or f32); scale <= 0 means 1/sqrt(D). */
+int         ada_flash_attention_forward(const AdaTensor* q, const AdaTensor* k,
+                                        const AdaTensor* v, float scale, int32_t causal,
+                                        AdaTensor* out, void* stream);
+
+/* _adaattn_cuda.compute_entropy (bindings.cpp:101-109): rows of `weights`
+ * (last dimension) -> entropy -sum w*log(w + 1e-10), f32 output with the
+ * leading dimensions. estimate_effective_rank (:114-118) is exp(mean of the
+ * last entropy dimension); determine_target_ranks (:123-135) maps effective
+ * ranks to int64 target ranks. */
+int         ada_compute_entropy(const AdaTensor* weights, float* entropy_out, void* stream);
+int         ada_estimate_effective_rank(const AdaTensor* weights, float* rank_out, void* stream);
+int         ada_determine_target_ranks(const float* effective_rank, int64_t n,
+                                       int64_t min_rank, int64_t max_rank, double threshold,
+                                       int64_t* ranks_out, void* stream);
+
+/* Test hook for failure detection: launches one block that waits on a device
+ * barrier nothing ever signals, bounded by `timeout_ns`; the wait gives up,
+ * records ADA_ERR_TIMEOUT in the status word and the kernel returns normally. */
+int         ada_debug_bounded_wait(uint64_t timeout_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ADAATTN_B200_H */

@@ -1,0 +1,408 @@
+"""CPU restatement of the AdaAttn attention-forward hot path (the oracle).
+
+TEST INFRASTRUCTURE ONLY. Nothing in the shipped package imports this module;
+the CUDA path is checked against it on the same seeded inputs.
+
+Each function restates one piece of the reference's algorithm in plain PyTorch
+CPU code, keeping the reference's dtype semantics (matmul / softmax / entropy in
+the tensor's own dtype, FP16-for-FP8 and so on) because decision parity depends
+on them. Citations are ``path:line`` inside the hkevin01/AdaAttn project.
+
+Pinning: ``tests/golden/make_golden.py`` runs the reference itself on seeded
+inputs and stores its decisions and outputs under ``tests/golden/``;
+``tests/test_oracle_golden.py`` checks this module against those fixtures and
+against the reference's own known-answer tests (entropy, randomized SVD).
+
+Precision codes follow the reference's ``_precision_distribution`` order
+(src/adaattn/attention/adaattn.py:480-485): FP32=0, FP16=1, BF16=2, FP8=3,
+plus AUTO=4 (computes in fp16, counted in slot 0 by the reference's
+``.get(precision, 0)``).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+__all__ = [
+    "FP32", "FP16", "BF16", "FP8", "AUTO", "PREC_NAMES", "compute_dtype",
+    "OracleConfig", "sample_stats", "decide", "analyze", "analyze_per_head",
+    "apply_masks", "dense_attention", "low_rank_attention", "adaptive_forward",
+    "module_forward",
+    "fp8_quantize_tiles", "fp8_dense_attention", "randomized_svd",
+    "rsvd_sketch", "E4M3_MAX", "FP8_TILE",
+]
+
+FP32, FP16, BF16, FP8, AUTO = 0, 1, 2, 3, 4
+PREC_NAMES = ("FP32", "FP16", "BF16", "FP8", "AUTO")
+
+# src/adaattn/attention/base.py:100-109 -- PrecisionMode.to_dtype; FP8 and AUTO
+# both compute in float16.
+_COMPUTE_DTYPE = {
+    FP32: torch.float32,
+    FP16: torch.float16,
+    BF16: torch.bfloat16,
+    FP8: torch.float16,
+    AUTO: torch.float16,
+}
+
+E4M3_MAX = 448.0
+FP8_TILE = 128
+
+
+def compute_dtype(prec: int) -> torch.dtype:
+    return _COMPUTE_DTYPE[prec]
+
+
+@dataclass
+class OracleConfig:
+    """Knobs of AdaAttention that steer the hot path.
+
+    Defaults mirror src/adaattn/attention/adaattn.py:57-79 and
+    src/adaattn/attention/base.py:203 (eps).
+    """
+
+    enable_adaptive_rank: bool = True
+    enable_adaptive_precision: bool = True
+    rank_threshold: float = 0.95
+    default_precision: int = FP16
+    allow_fp8: bool = False
+    causal: bool = False
+    eps: float = 1e-6
+
+
+def sample_stats(q: torch.Tensor, k: torch.Tensor, scale: float, eps: float
+                 ) -> Tuple[float, float, float, int]:
+    """Statistics of the analyzer sample, computed in the inputs' dtype.
+
+    Follows src/adaattn/attention/adaattn.py:248-275: the first
+    S = min(64, Nq, Nk) queries and keys, scores = q_s k_s^T * scale,
+    softmax, per-row entropy -sum p*log(p+eps), normalised by log(S) and
+    averaged over every (batch, head, row) of the tensors passed in.
+
+    Returns (normalized_entropy, max|score|, max prob, S).
+    """
+    n_q, n_k = q.shape[2], k.shape[2]
+    s = min(64, n_q, n_k)
+    scores = torch.matmul(q[:, :, :s], k[:, :, :s].transpose(-2, -1)) * scale
+    probs = F.softmax(scores, dim=-1)
+    row_entropy = -(probs * torch.log(probs + eps)).sum(dim=-1)
+    ne = (row_entropy / math.log(s)).mean().item()
+    return ne, scores.abs().max().item(), probs.max().item(), s
+
+
+def decide(ne: float, max_score: float, max_prob: float, cfg: OracleConfig
+           ) -> Tuple[bool, int]:
+    """Rank and precision ladder of src/adaattn/attention/adaattn.py:268-287.
+
+    NaN statistics compare False everywhere, exactly as Python floats do.
+    """
+    low_rank = bool(cfg.enable_adaptive_rank and ne < cfg.rank_threshold)
+    if max_score > 50.0 or max_prob > 0.95:
+        prec = FP32
+    elif ne > 0.8:
+        prec = FP8 if cfg.allow_fp8 else FP16
+    elif ne < 0.3:
+        prec = BF16
+    else:
+        prec = cfg.default_precision
+    if not cfg.enable_adaptive_precision:
+        prec = cfg.default_precision
+    return low_rank, prec
+
+
+def analyze(q: torch.Tensor, k: torch.Tensor, cfg: OracleConfig, scale: float
+            ) -> dict:
+    """One decision for the whole call (the reference's own granularity).
+
+    src/adaattn/attention/adaattn.py:228-289; effective rank is
+    ne * min(Nq, Nk) (:266).
+    """
+    ne, ms, mp, _ = sample_stats(q, k, scale, cfg.eps)
+    low_rank, prec = decide(ne, ms, mp, cfg)
+    return {
+        "low_rank": low_rank, "precision": prec, "ne": ne,
+        "max_score": ms, "max_prob": mp,
+        "effective_rank": ne * min(q.shape[2], k.shape[2]),
+    }
+
+
+def analyze_per_head(q: torch.Tensor, k: torch.Tensor, cfg: OracleConfig,
+                     scale: float) -> dict:
+    """The reference analyzer applied to every (b, h) slice on its own.
+
+    Returns tensors [B, H]: low_rank (bool), precision (int), ne, max_score,
+    max_prob (float64, the values the reference's ``.item()`` would give).
+    """
+    b_sz, h_sz = q.shape[0], q.shape[1]
+    low = torch.zeros(b_sz, h_sz, dtype=torch.bool)
+    prec = torch.zeros(b_sz, h_sz, dtype=torch.int32)
+    ne = torch.zeros(b_sz, h_sz, dtype=torch.float64)
+    ms = torch.zeros_like(ne)
+    mp = torch.zeros_like(ne)
+    for b in range(b_sz):
+        for h in range(h_sz):
+            d = analyze(q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1], cfg, scale)
+            low[b, h] = d["low_rank"]
+            prec[b, h] = d["precision"]
+            ne[b, h], ms[b, h], mp[b, h] = d["ne"], d["max_score"], d["max_prob"]
+    return {"low_rank": low, "precision": prec, "ne": ne, "max_score": ms,
+            "max_prob": mp}
+
+
+def apply_masks(scores: torch.Tensor, causal: bool,
+                attention_mask: Optional[torch.Tensor], dt: torch.dtype
+                ) -> torch.Tensor:
+    """Causal and user masks of src/adaattn/attention/adaattn.py:312-329.
+
+    Causal is top-left aligned: key j is hidden from query i when j > i.
+    A 2-D mask is [B, Nk], 3-D is [B, Nq, Nk], 4-D is used as given. Boolean
+    masks keep True positions; float masks are added in the compute dtype.
+    """
+    if causal:
+        n_q, n_k = scores.shape[-2], scores.shape[-1]
+        hide = torch.ones(n_q, n_k, dtype=torch.bool).triu(1)
+        scores = scores.masked_fill(hide, float("-inf"))
+    if attention_mask is not None:
+        m = attention_mask
+        if m.ndim == 2:
+            m = m[:, None, None, :]
+        elif m.ndim == 3:
+            m = m[:, None]
+        if m.dtype == torch.bool:
+            scores = scores.masked_fill(~m, float("-inf"))
+        else:
+            scores = scores + m.to(dt)
+    return scores
+
+
+def _softmax_in_precision(scores: torch.Tensor, prec: int, dt: torch.dtype
+                          ) -> torch.Tensor:
+    # adaattn.py:331-334 / :386-389: FP16 and FP8 take the softmax in fp32 and
+    # cast back; FP32, BF16 and AUTO take it in the compute dtype itself.
+    if prec in (FP16, FP8):
+        return F.softmax(scores.float(), dim=-1).to(dt)
+    return F.softmax(scores, dim=-1)
+
+
+def dense_attention(q, k, v, prec: int, scale: float, causal: bool,
+                    attention_mask=None) -> torch.Tensor:
+    """Dense branch, src/adaattn/attention/adaattn.py:291-339 (eval mode).
+
+    Scores are clamped to the fp16 range for FP16 and FP8 (:309-310).
+    """
+    dt = compute_dtype(prec)
+    qc, kc, vc = q.to(dt), k.to(dt), v.to(dt)
+    scores = torch.matmul(qc, kc.transpose(-2, -1)) * scale
+    if prec in (FP16, FP8):
+        scores = torch.clamp(scores, min=-65504, max=65504)
+    scores = apply_masks(scores, causal, attention_mask, dt)
+    probs = _softmax_in_precision(scores, prec, dt)
+    return torch.matmul(probs, vc).to(q.dtype)
+
+
+def low_rank_attention(q, k, v, w_down: torch.Tensor, prec: int, scale: float,
+                       causal: bool, attention_mask=None) -> torch.Tensor:
+    """Low-rank branch, src/adaattn/attention/adaattn.py:341-394 (eval mode).
+
+    q and k go through the learned head-dim projection ``rank_proj_down``
+    (weight [r, D], no bias) in the inputs' dtype, then scores use the
+    module's 1/sqrt(D) scale on the r-dimensional products; V stays full
+    width. No clamp on this branch.
+    """
+    dt = compute_dtype(prec)
+    w = w_down.to(q.dtype)
+    q_low = F.linear(q, w).to(dt)
+    k_low = F.linear(k, w).to(dt)
+    vc = v.to(dt)
+    scores = torch.matmul(q_low, k_low.transpose(-2, -1)) * scale
+    scores = apply_masks(scores, causal, attention_mask, dt)
+    probs = _softmax_in_precision(scores, prec, dt)
+    return torch.matmul(probs, vc).to(q.dtype)
+
+
+def _slice_mask(mask, b: int, h: int):
+    if mask is None:
+        return None
+    if mask.ndim in (2, 3):
+        return mask[b:b + 1]
+    return mask[b:b + 1, (h if mask.shape[1] > 1 else 0):][:, :1]
+
+
+def adaptive_forward(q, k, v, cfg: OracleConfig, scale: float,
+                     w_down: Optional[torch.Tensor] = None,
+                     granularity: str = "head", attention_mask=None,
+                     fp8_mode: str = "reference") -> Tuple[torch.Tensor, dict]:
+    """The adaptive dispatcher, src/adaattn/attention/adaattn.py:462-504.
+
+    granularity "global" is the reference's own behaviour: one decision per
+    call. "head" applies the same analyzer and branch to each (b, h) slice.
+    fp8_mode "reference" computes FP8 heads in fp16 like base.py:106;
+    "e4m3" uses the tile-scaled E4M3 restatement below.
+    Returns (output [B,H,Nq,D], decisions).
+    """
+    def run(qs, ks, vs, low, prec, mask):
+        if low and w_down is not None:
+            if prec == FP8 and fp8_mode == "e4m3":
+                return fp8_dense_attention(qs, ks, vs, scale, cfg.causal, mask,
+                                           w_down=w_down)
+            return low_rank_attention(qs, ks, vs, w_down, prec, scale,
+                                      cfg.causal, mask)
+        if prec == FP8 and fp8_mode == "e4m3":
+            return fp8_dense_attention(qs, ks, vs, scale, cfg.causal, mask)
+        return dense_attention(qs, ks, vs, prec, scale, cfg.causal, mask)
+
+    if granularity == "global":
+        d = analyze(q, k, cfg, scale)
+        out = run(q, k, v, d["low_rank"], d["precision"], attention_mask)
+        return out, d
+    d = analyze_per_head(q, k, cfg, scale)
+    out = torch.empty(q.shape[0], q.shape[1], q.shape[2], v.shape[3],
+                      dtype=q.dtype)
+    for b in range(q.shape[0]):
+        for h in range(q.shape[1]):
+            out[b:b + 1, h:h + 1] = run(
+                q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1], v[b:b + 1, h:h + 1],
+                bool(d["low_rank"][b, h]), int(d["precision"][b, h]),
+                _slice_mask(attention_mask, b, h))
+    return out, d
+
+
+def module_forward(query, key, value, state_dict: dict, num_heads: int,
+                   cfg: OracleConfig, granularity: str = "global",
+                   attention_mask=None, fp8_mode: str = "reference"
+                   ) -> Tuple[torch.Tensor, dict]:
+    """AdaAttention.forward in eval mode, src/adaattn/attention/adaattn.py:396-460.
+
+    Projections E->E, split into heads [B, H, N, D], the adaptive core, merge
+    heads, output projection. The flash_attn branch (:421-445) is never taken
+    on CPU tensors, so it is not restated.
+    """
+    sd = state_dict
+    b_sz, n_q, e = query.shape
+    n_k = key.shape[1]
+    d = e // num_heads
+
+    def proj(x, name):
+        return F.linear(x, sd[f"{name}.weight"], sd.get(f"{name}.bias"))
+
+    q = proj(query, "q_proj").view(b_sz, n_q, num_heads, d).transpose(1, 2)
+    k = proj(key, "k_proj").view(b_sz, n_k, num_heads, d).transpose(1, 2)
+    v = proj(value, "v_proj").view(b_sz, n_k, num_heads, d).transpose(1, 2)
+    w_down = sd.get("rank_proj_down.weight")
+    out, dec = adaptive_forward(q, k, v, cfg, 1.0 / math.sqrt(d), w_down,
+                                granularity, attention_mask, fp8_mode)
+    out = out.transpose(1, 2).contiguous().view(b_sz, n_q, e)
+    return proj(out, "out_proj"), dec
+
+
+# --------------------------------------------------------------------------
+# FP8-E4M3 restatement (the build's real FP8 heads).
+#
+# The reference's "FP8" computes in fp16 (base.py:106), so a real E4M3 kernel
+# needs its own oracle: the same per-tile quantisation the kernel performs,
+# followed by fp32 arithmetic. Scheme:
+#   Q: one scale per (b, h, 128-row query tile), K: one per (b, h, 128-row key
+#   tile), V: one per (b, h); scale = amax / 448 (1 when amax is 0),
+#   x8 = e4m3(x / scale) (round to nearest even, |x/scale| <= 448).
+#   S_j = (Q8 K8_j^T) * sq * sk_j * softmax_scale; running row max m;
+#   P8 = e4m3(exp(S_j - m) * 448); O += P8 V8; l += sum(exp(S_j - m));
+#   out = O * sv / (448 * l).
+# --------------------------------------------------------------------------
+
+def fp8_quantize_tiles(x: torch.Tensor, tile: Optional[int] = FP8_TILE
+                       ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-(b, h, row-tile) E4M3 quantisation of x [B, H, N, D] (fp32 math).
+
+    tile=None gives one scale per (b, h). Returns (dequantised fp32 values,
+    scales [B, H, n_tiles]).
+    """
+    xf = x.float()
+    b_sz, h_sz, n, d = xf.shape
+    t = n if tile is None else tile
+    n_tiles = max(1, -(-n // t))
+    pad = n_tiles * t - n
+    xp = F.pad(xf, (0, 0, 0, pad)) if pad else xf
+    xt = xp.view(b_sz, h_sz, n_tiles, t, d)
+    amax = xt.abs().amax(dim=(-1, -2))
+    scale = torch.where(amax > 0, amax / E4M3_MAX, torch.ones_like(amax))
+    q8 = (xt / scale[..., None, None]).to(torch.float8_e4m3fn)
+    deq = q8.float() * scale[..., None, None]
+    return deq.view(b_sz, h_sz, n_tiles * t, d)[:, :, :n], scale
+
+
+def fp8_dense_attention(q, k, v, scale: float, causal: bool,
+                        attention_mask=None, w_down=None,
+                        block: int = FP8_TILE) -> torch.Tensor:
+    """Tile-scaled E4M3 attention, computed block by block like the kernel.
+
+    With w_down given, q and k are first projected (in the inputs' dtype,
+    as adaattn.py:357-358) and the projected values are quantised.
+    """
+    if w_down is not None:
+        w = w_down.to(q.dtype)
+        q = F.linear(q, w)
+        k = F.linear(k, w)
+    qd, _ = fp8_quantize_tiles(q)
+    kd, _ = fp8_quantize_tiles(k)
+    vd, _ = fp8_quantize_tiles(v, tile=None)
+    n_q, n_k = qd.shape[2], kd.shape[2]
+    scores = torch.matmul(qd, kd.transpose(-2, -1)) * scale
+    scores = apply_masks(scores, causal, attention_mask, torch.float32)
+    out = torch.zeros(qd.shape[0], qd.shape[1], n_q, vd.shape[3])
+    m = torch.full((qd.shape[0], qd.shape[1], n_q, 1), float("-inf"))
+    l = torch.zeros_like(m)
+    for j0 in range(0, n_k, block):
+        s = scores[..., j0:j0 + block]
+        m_new = torch.maximum(m, s.amax(dim=-1, keepdim=True))
+        alpha = torch.where(m_new == float("-inf"), torch.ones_like(m),
+                            torch.exp(m - m_new))
+        p = torch.where(m_new == float("-inf"), torch.zeros_like(s),
+                        torch.exp(s - m_new))
+        p8 = (p * E4M3_MAX).to(torch.float8_e4m3fn).float()
+        out = out * alpha + torch.matmul(p8, vd[:, :, j0:j0 + block])
+        l = l * alpha + p.sum(dim=-1, keepdim=True)
+        m = m_new
+    return (out / (E4M3_MAX * l)).to(q.dtype)
+
+
+# --------------------------------------------------------------------------
+# Randomized SVD, src/adaattn/linalg/low_rank.py:56-109.
+# --------------------------------------------------------------------------
+
+def randomized_svd(a: torch.Tensor, rank: int, omega: torch.Tensor,
+                   n_power: int = 2, qr: str = "householder"
+                   ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Halko-style truncated SVD with the Gaussian sketch passed in.
+
+    The reference draws omega [..., n, k] with k = min(rank + 10, min(m, n))
+    from torch.randn (low_rank.py:80-83); passing it makes the algorithm
+    deterministic. qr="householder" is the reference's torch.linalg.qr
+    (:93); qr="cholesky" is CholeskyQR (Q = Y R^-1 with R = chol(Y^T Y)^T),
+    the form the GPU path uses.
+    """
+    y = torch.matmul(a, omega)
+    for _ in range(n_power):
+        y = torch.matmul(a, torch.matmul(a.transpose(-2, -1), y))
+    if qr == "householder":
+        qm, _ = torch.linalg.qr(y)
+    else:
+        g = torch.matmul(y.transpose(-2, -1), y)
+        r_up = torch.linalg.cholesky(g).transpose(-2, -1)
+        qm = torch.linalg.solve_triangular(r_up, y, upper=True, left=False)
+    bm = torch.matmul(qm.transpose(-2, -1), a)
+    ub, s, vh = torch.linalg.svd(bm, full_matrices=False)
+    u = torch.matmul(qm, ub)
+    return u[..., :rank], s[..., :rank], vh[..., :rank, :]
+
+
+def rsvd_sketch(shape_batch, n: int, rank: int, m: int, seed: int,
+                oversample: int = 10, dtype=torch.float32) -> torch.Tensor:
+    """Seeded Gaussian sketch of the reference's shape [..., n, k]."""
+    k = min(rank + oversample, min(m, n))
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape_batch, n, k, generator=g, dtype=dtype)

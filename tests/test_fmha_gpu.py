@@ -1,0 +1,166 @@
+"""Attention kernels vs the CPU oracle, one fixed precision per call.
+
+Covers the tensor-core kernels (bf16 / fp16 / E4M3; dense and low rank;
+head dims 32..128, padded where needed), the fp32 CUDA-core kernel, causal
+and non-causal, ragged and tiny sequence lengths, Nq != Nk, masks and
+strided [B, N, H, D] views. Tolerances: tests/parity.py.
+"""
+
+import math
+
+import pytest
+import torch
+
+import oracle as O
+from adaattn_b200 import PrecisionMode, attention_forward
+from parity import check_head
+
+pytestmark = pytest.mark.gpu
+
+PM = {O.FP32: PrecisionMode.FP32, O.FP16: PrecisionMode.FP16, O.BF16: PrecisionMode.BF16,
+      O.FP8: PrecisionMode.FP8, O.AUTO: PrecisionMode.AUTO}
+
+
+def _inputs(b, h, nq, nk, d, dtype, seed=0, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(b, h, nq, d, generator=g) * scale).to(dtype)
+    k = (torch.randn(b, h, nk, d, generator=g) * scale).to(dtype)
+    v = torch.randn(b, h, nk, d, generator=g).to(dtype)
+    return q, k, v
+
+
+def _w_down(d, r, dtype, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.empty(r, d)
+    torch.nn.init.orthogonal_(w, generator=g)
+    return w.to(dtype)
+
+
+def _run(q, k, v, prec, low, causal, dev, mask=None, w=None, fp8_mode="e4m3"):
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d)
+    out = attention_forward(q.to(dev), k.to(dev), v.to(dev), scale=scale, causal=causal,
+                            static_precision=PM[prec], static_low_rank=low,
+                            w_down=None if w is None else w.to(dev),
+                            attention_mask=None if mask is None else mask.to(dev),
+                            fp8_mode=fp8_mode)
+    torch.cuda.synchronize()
+    return out.cpu(), scale
+
+
+DENSE_CASES = [
+    # (dtype, prec, d, nq, nk)
+    (torch.bfloat16, O.BF16, 128, 256, 256),
+    (torch.bfloat16, O.BF16, 128, 300, 300),
+    (torch.bfloat16, O.BF16, 64, 200, 200),
+    (torch.bfloat16, O.BF16, 128, 17, 17),
+    (torch.bfloat16, O.BF16, 128, 1, 1),
+    (torch.bfloat16, O.BF16, 128, 64, 333),
+    (torch.bfloat16, O.BF16, 128, 333, 64),
+    (torch.float16, O.FP16, 128, 256, 256),
+    (torch.float16, O.FP16, 64, 130, 130),
+    (torch.bfloat16, O.FP16, 128, 256, 256),   # cast in the prep kernel
+    (torch.float32, O.FP16, 64, 256, 256),
+    (torch.float32, O.BF16, 128, 192, 192),
+    (torch.float32, O.AUTO, 64, 128, 128),
+    (torch.float32, O.FP32, 64, 256, 256),     # CUDA-core path
+    (torch.bfloat16, O.FP32, 128, 130, 130),
+    (torch.float32, O.FP32, 32, 77, 140),
+    (torch.float32, O.FP16, 96, 100, 100),     # head dim padded to 128
+    (torch.bfloat16, O.BF16, 32, 150, 150),    # head dim padded to 64
+]
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("case", DENSE_CASES, ids=lambda c: f"{c[0]}-p{c[1]}-d{c[2]}-{c[3]}x{c[4]}")
+def test_dense_static(case, causal, cuda_device):
+    dtype, prec, d, nq, nk = case
+    q, k, v = _inputs(2, 3, nq, nk, d, dtype)
+    out, scale = _run(q, k, v, prec, False, causal, cuda_device)
+    for b in range(2):
+        for h in range(3):
+            check_head(out[b:b + 1, h:h + 1], q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1],
+                       v[b:b + 1, h:h + 1], prec, False, scale, causal, label=f"b{b}h{h}")
+
+
+LOW_CASES = [
+    (torch.bfloat16, O.FP16, 128, 64, 256),
+    (torch.bfloat16, O.BF16, 128, 64, 300),
+    (torch.bfloat16, O.FP32, 128, 64, 200),
+    (torch.float32, O.FP16, 64, 32, 256),
+    (torch.float32, O.FP32, 64, 32, 129),
+]
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("case", LOW_CASES, ids=lambda c: f"{c[0]}-p{c[1]}-d{c[2]}-r{c[3]}-n{c[4]}")
+def test_low_rank_static(case, causal, cuda_device):
+    dtype, prec, d, r, n = case
+    q, k, v = _inputs(1, 2, n, n, d, dtype, seed=3)
+    w = _w_down(d, r, dtype)
+    out, scale = _run(q, k, v, prec, True, causal, cuda_device, w=w)
+    for h in range(2):
+        check_head(out[:, h:h + 1], q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], prec, True,
+                   scale, causal, w_down=w, label=f"h{h}")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("n", [128, 256, 333])
+@pytest.mark.parametrize("low", [False, True])
+def test_fp8_e4m3(n, causal, low, cuda_device):
+    q, k, v = _inputs(1, 2, n, n, 128, torch.bfloat16, seed=5, scale=0.5)
+    w = _w_down(128, 64, torch.bfloat16) if low else None
+    out, scale = _run(q, k, v, O.FP8, low, causal, cuda_device, w=w)
+    for h in range(2):
+        check_head(out[:, h:h + 1], q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], O.FP8, low,
+                   scale, causal, w_down=w, label=f"h{h}")
+
+
+def test_fp8_reference_mode_is_fp16(cuda_device):
+    q, k, v = _inputs(1, 2, 200, 200, 128, torch.bfloat16, seed=6)
+    out, scale = _run(q, k, v, O.FP8, False, True, cuda_device, fp8_mode="fp16")
+    check_head(out, q, k, v, O.FP8, False, scale, True, fp8_mode="fp16")
+
+
+@pytest.mark.parametrize("prec,dtype", [(O.BF16, torch.bfloat16), (O.FP16, torch.float32),
+                                        (O.FP32, torch.float32)])
+def test_masks(prec, dtype, cuda_device):
+    q, k, v = _inputs(2, 2, 96, 160, 64, dtype, seed=7)
+    g = torch.Generator().manual_seed(8)
+    keep = torch.rand(2, 160, generator=g) > 0.3
+    keep[:, 0] = True
+    add = torch.randn(2, 96, 160, generator=g)
+    for mask in (keep, add):
+        out, scale = _run(q, k, v, prec, False, False, cuda_device, mask=mask)
+        for b in range(2):
+            for h in range(2):
+                check_head(out[b:b + 1, h:h + 1], q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1],
+                           v[b:b + 1, h:h + 1], prec, False, scale, False, mask=mask[b:b + 1],
+                           label=f"mask{mask.dtype}-b{b}h{h}")
+
+
+def test_strided_bnhd_views(cuda_device):
+    """[B, N, H, D] buffers passed as transposed views; output written in place."""
+    b, n, h, d = 2, 257, 4, 128
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(3, b, n, h, d, generator=g).to(torch.bfloat16)
+    qv, kv_, vv = (x[i].to(cuda_device).transpose(1, 2) for i in range(3))
+    merged = torch.empty(b, n, h, d, dtype=torch.bfloat16, device=cuda_device)
+    attention_forward(qv, kv_, vv, scale=d ** -0.5, causal=True,
+                      static_precision=PrecisionMode.BF16, out=merged.transpose(1, 2))
+    torch.cuda.synchronize()
+    got = merged.transpose(1, 2).cpu()
+    q, k, v = (x[i].transpose(1, 2) for i in range(3))
+    check_head(got, q, k, v, O.BF16, False, d ** -0.5, True)
+
+
+def test_fully_masked_row_is_nan_like_reference(cuda_device):
+    q, k, v = _inputs(1, 1, 8, 16, 64, torch.float32, seed=10)
+    keep = torch.ones(1, 8, 16, dtype=torch.bool)
+    keep[0, 3] = False
+    for prec in (O.FP32, O.FP16):
+        out, scale = _run(q, k, v, prec, False, False, cuda_device, mask=keep)
+        ref = O.dense_attention(q, k, v, prec, scale, False, keep)
+        assert torch.isnan(ref[0, 0, 3]).all()
+        assert torch.isnan(out[0, 0, 3]).all()
+        assert not torch.isnan(out[0, 0, :3]).any()
