@@ -203,11 +203,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="profiling only: smaller batch than the B8 workload")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="profiling only: fewer heads than the H32 workload")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
     from adaattn_b200.workloads import WORKLOADS, make_qkv
-    workload = WORKLOADS["dense_bf16"]
+    workload = WORKLOADS["dense_bf16"].scaled(batch=args.batch, heads=args.heads)
     if args.impl == "reference":
         return run_reference(args, workload)
 

@@ -15,7 +15,7 @@ import oracle as O
 from adaattn_b200 import AdaAttention, PrecisionMode, analyze, attention_forward
 from adaattn_b200.core import possible_precisions
 from golden_util import CASE_NAMES, PREC_CODE, inputs, load, module_kwargs, oracle_config
-from parity import check_head, near_threshold
+from parity import check_head, output_ulp
 
 pytestmark = pytest.mark.gpu
 
@@ -72,7 +72,7 @@ def test_golden_outputs(name, granularity, cuda_device):
                     g = golden[sl].float()
                     got = full[:, :, rows].float()
                     mm = max(1.0, g.abs().max().item())
-                    bar = (1e-5 if p == O.FP32 else 2e-3) * mm
+                    bar = ((1e-5 if p == O.FP32 else 2e-3) + output_ulp(golden.dtype)) * mm
                     err = (got - g).abs().max().item() if g.numel() else 0.0
                     both_nan = torch.isnan(g).all() and torch.isnan(got).all()
                     assert both_nan or err <= bar, f"{label}: {err:.3e} > {bar:.3e} vs reference"
@@ -133,8 +133,11 @@ def test_module_per_head_mode(name, cuda_device):
         m.rank_proj_down.weight.data.copy_(rec["w_down"].to(cuda_device))
     out, table = m.attention_core(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device))
     cfg = oracle_config(rec)
-    want, dec = O.adaptive_forward(q, k, v, cfg, rec["scale"], rec["w_down"], "head")
-    prec, low = table.precision.cpu(), table.low_rank.cpu()
+    if table is None:  # decisions fixed by the configuration (no analyzer pass)
+        prec = torch.full((rec["batch"], h), m.default_precision.code)
+        low = torch.zeros(rec["batch"], h, dtype=torch.bool)
+    else:
+        prec, low = table.precision.cpu(), table.low_rank.cpu()
     out = out.cpu()
     for b in range(rec["batch"]):
         for hh in range(h):
