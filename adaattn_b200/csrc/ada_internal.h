@@ -144,6 +144,7 @@ struct TcLaunch {
     const float* k_scale;  // e4m3: [B,H,nt_k]
     const float* v_scale;  // e4m3: [B,H]
     int64_t nt_q, nt_k;
+    int* work_counter;  // zeroed work-item counter (dynamic scheduling), or nullptr (static striding)
     unsigned int* status;
     uint64_t timeout_ns;
 };

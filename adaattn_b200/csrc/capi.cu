@@ -186,8 +186,12 @@ struct Plan {
     int64_t nt_q, nt_k;
     size_t off16q, off16k, off16v, off32q, off32k, off8q, off8k, off8v;
     size_t off_amax_q, off_amax_k, off_amax_v, off_sq, off_sk, off_sv;
-    size_t total;
+    size_t required;      // bytes the operand regions need
+    size_t off_counters;  // work-item counters of the tensor-core launches
+    size_t total;         // required + counters
 };
+
+constexpr int kMaxCounters = 16;
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -299,7 +303,9 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
         P->off_sv = off;
         off = align256(off + static_cast<size_t>(BH) * 4);
     }
-    P->total = off;
+    P->required = off;
+    P->off_counters = off;
+    P->total = align256(off + kMaxCounters * sizeof(int));
     return ADA_OK;
 }
 
@@ -450,7 +456,10 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
     if (out->shape[0] != P.B || out->shape[1] != P.H || out->shape[2] != P.Nq || out->shape[3] != P.D)
         return fail(ADA_ERR_SHAPE, "out must be [B,H,Nq,D]");
     if ((rc = check_mask(mask, P))) return rc;
-    if (P.total > 0 && (workspace == nullptr || workspace_bytes < P.total))
+    // Without a workspace the tensor-core launches stride statically over
+    // their work items; with one they share dynamically scheduled counters.
+    const bool have_ws = workspace != nullptr && workspace_bytes >= P.total;
+    if (P.required > 0 && !have_ws)
         return fail(ADA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", P.total, workspace_bytes);
     if (P.B * P.H == 0 || P.Nq == 0) return ADA_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -518,6 +527,10 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
 
     // ---- tensor-core launches ---------------------------------------------
     const float log2e = 1.4426950408889634f;
+    int* counters = have_ws ? reinterpret_cast<int*>(ws + P.off_counters) : nullptr;
+    int next_counter = 0;
+    if (counters != nullptr && cudaMemsetAsync(counters, 0, kMaxCounters * sizeof(int), s) != cudaSuccess)
+        return fail(ADA_ERR_CUDA, "clearing the work counters failed");
     auto base_tc = [&](TcLaunch& L) {
         std::memset(&L, 0, sizeof(L));
         L.B = P.B;
@@ -536,6 +549,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         L.timeout_ns = wait_timeout_ns();
         L.nt_q = P.nt_q;
         L.nt_k = P.nt_k;
+        L.work_counter = (counters != nullptr && next_counter < kMaxCounters) ? counters + next_counter++ : nullptr;
     };
     for (int cdi = 0; cdi < 2; ++cdi) {
         const int cd = cdi == 0 ? ADA_F16 : ADA_BF16;

@@ -1,29 +1,59 @@
 // K2: fused attention forward on the sm_100a tensor cores.
 //
-// One CTA owns two 128-row query tiles of one (b, h) and streams 128-key
-// blocks of K and V through a shared-memory ring filled by TMA. S = Q K^T and
-// O += P V run as tcgen05 MMAs with fp32 accumulators in tensor memory; the
-// score block never leaves the SM. Warp roles (320 threads):
+// Persistent CTAs (one per SM) walk a list of work items; an item is two
+// 128-row query tiles of one (b, h). Items are ordered head-major (the tiles
+// of one head run side by side, so its K and V stream from L2) and, within a
+// head, heavy-first (late tiles have more keys under causal masking); CTA c
+// takes items c, c + grid, c + 2*grid, ...
+//
+// Per item, 128-key blocks of K and V stream through a shared-memory ring
+// filled by TMA. S = Q K^T (SS) and O += P V (TS: P read from tensor memory)
+// run as tcgen05 MMAs with fp32 accumulators in TMEM; the score block never
+// leaves the SM. Warp roles (320 threads):
 //   warps 0-3 / 4-7  softmax for query tile 0 / 1: read S from TMEM (one row
 //                    per thread), online softmax in registers, write P (16-bit
-//                    or E4M3) back into the S columns, rescale O when the
-//                    running maximum moves, final normalisation and store.
-//   warp 8           TMA producer (Q tiles once, then K_j, V_j per block).
+//                    or E4M3) over the S columns, rescale O when the running
+//                    maximum moves, final normalisation and store.
+//   warp 8           TMA producer (Q tiles per item, double buffered; then
+//                    K_j, V_j through the ring).
 //   warp 9           TMEM allocation and the single-thread MMA issuer.
 // The two query tiles ping-pong: while one tile's softmax runs, the tensor
-// core works on the other tile's products.
+// core works on the other tile's products. Across items the producer and the
+// MMA issuer run ahead, so the next item's first products overlap this item's
+// final normalisation and stores.
 //
 // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+DV) O1 [256+DV,256+2DV).
-// Every wait is bounded (ada::mbar_wait); a timeout raises the CTA's abort
-// flag and ADA_ERR_TIMEOUT in the status word instead of hanging.
+// Barrier phases are tracked by running counters across items. Every wait is
+// bounded (ada::mbar_wait); a timeout raises the CTA's abort flag and
+// ADA_ERR_TIMEOUT in the status word instead of hanging.
 #include "ada_common.cuh"
 #include "ada_internal.h"
 
 namespace ada {
 namespace {
 
-constexpr int kThreadsTc = 320;
-constexpr int kSmemTarget = 200 * 1024;
+// Three warpgroups: two softmax warpgroups and one for TMA / MMA (two of its
+// warps idle). Launched at 168 registers per thread (the cap for 12 warps);
+// the TMA/MMA warpgroup gives registers back and the softmax warpgroups take
+// them: 2 * 128 * 208 + 128 * 88 = 384 * 168.
+constexpr int kThreadsTc = 384;
+constexpr int kLaunchRegs = 168;
+constexpr int kSoftmaxRegs = 208;
+constexpr int kOtherRegs = 88;
+// Threads that read each broadcast work item: the MMA issuer and the 256
+// softmax threads.
+constexpr int kItemConsumers = 1 + 256;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreadsTc * kLaunchRegs,
+              "register split exceeds the launch pool");
+// Pairs of scores (of every 8 pairs) whose exponential runs as a polynomial
+// on the FMA pipe; the rest use MUFU ex2.
+#ifndef ADA_EXP2_POLY_PAIRS
+#define ADA_EXP2_POLY_PAIRS 0
+#endif
+constexpr int kPolyPairs = ADA_EXP2_POLY_PAIRS;
+// Dynamic shared memory budget: 227 KB per CTA minus alignment slack and the
+// barrier block.
+constexpr int kSmemBudget = 232448 - 1024 - 512;
 
 template <int ELT, int DQK, int DV>
 struct TcCfg {
@@ -36,11 +66,12 @@ struct TcCfg {
     static constexpr int V_ATOMS = DV * EB / 128;
     static_assert(QK_ATOMS >= 1 && QK_ATOMS * 128 == DQK * EB, "DQK row must be whole 128-byte atoms");
     static_assert(V_ATOMS >= 1 && V_ATOMS * 128 == DV * EB, "DV row must be whole 128-byte atoms");
-    static constexpr int Q_BYTES = BM * DQK * EB;
+    static constexpr int Q_BYTES = BM * DQK * EB;         // one query tile
+    static constexpr int QBUF_BYTES = 2 * Q_BYTES;        // both tiles of one item
     static constexpr int K_BYTES = BN * DQK * EB;
     static constexpr int V_BYTES = BN * DV * EB;
     static constexpr int STAGE_BYTES = K_BYTES > V_BYTES ? K_BYTES : V_BYTES;
-    static constexpr int NSTAGE_RAW = (kSmemTarget - 2 * Q_BYTES) / STAGE_BYTES;
+    static constexpr int NSTAGE_RAW = (kSmemBudget - 2 * QBUF_BYTES) / STAGE_BYTES;
     static constexpr int NSTAGE = NSTAGE_RAW > 8 ? 8 : NSTAGE_RAW;
     static_assert(NSTAGE >= 2, "ring too small");
     static constexpr int MMA_K = (ELT == 2) ? 32 : 16;   // elements per MMA k-step
@@ -49,22 +80,58 @@ struct TcCfg {
     static constexpr uint32_t FMT = (ELT == 1) ? 1u : 0u; // bf16 = 1, f16 = 0, e4m3 = 0
     static constexpr uint32_t IDESC_QK = make_idesc(FMT, FMT, 0, 0, 128, BN);
     static constexpr uint32_t IDESC_PV = make_idesc(FMT, FMT, 0, 1, 128, DV);
-    static constexpr int SMEM_BYTES = 2 * Q_BYTES + NSTAGE * STAGE_BYTES + 1024 /*align*/ + 256;
+    static constexpr int SMEM_BYTES = 2 * QBUF_BYTES + NSTAGE * STAGE_BYTES + 1024 + 512;
 };
 
 struct __align__(8) TcBarriers {
-    uint64_t q_full;
+    uint64_t q_full[2];
+    uint64_t q_empty[2];
     uint64_t s_full[2];
     uint64_t p_full[2];
     uint64_t o_full[2];
     uint64_t teardown;
+    uint64_t item_full[4];   // work-item broadcast ring (producer -> consumers)
+    uint64_t item_empty[4];
+    int64_t item_q[4];
     uint64_t kv_full[8];
     uint64_t kv_empty[8];
     uint32_t tmem_base;
     int abort_flag;
 };
 
+// One work item: the (b, h) slice and the pair of query tiles, with the
+// number of key blocks each tile needs.
+struct Item {
+    int64_t bh;
+    int b, h, qtp;
+    int n_t[2];
+    int nblk;
+};
+
 __device__ __forceinline__ int ceil_div_i(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+__device__ __forceinline__ Item decode_item(const TcLaunch& L, int64_t it, int n_qtp, int nkb) {
+    Item w;
+    w.bh = it / n_qtp;
+    w.qtp = n_qtp - 1 - static_cast<int>(it % n_qtp);
+    w.b = static_cast<int>(w.bh / L.H);
+    w.h = static_cast<int>(w.bh % L.H);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const int64_t r0 = (static_cast<int64_t>(w.qtp) * 2 + t) * 128;
+        if (r0 >= L.Nq) {
+            w.n_t[t] = 0;
+        } else if (L.causal) {
+            const int64_t r_last = (r0 + 127 < L.Nq - 1) ? r0 + 127 : L.Nq - 1;
+            const int need = static_cast<int>(r_last / 128) + 1;
+            w.n_t[t] = need < nkb ? need : nkb;
+        } else {
+            w.n_t[t] = nkb;
+        }
+    }
+    w.nblk = w.n_t[0] > w.n_t[1] ? w.n_t[0] : w.n_t[1];
+    return w;
+}
 
 template <int ELT>
 __device__ __forceinline__ void issue_mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
@@ -97,55 +164,68 @@ __device__ __forceinline__ void teardown_wait(uint32_t bar, uint32_t parity, uin
     }
 }
 
+// The producer picks the CTA's next work item this launch serves: from the
+// shared counter (dynamic: a CTA that finishes early takes more items, which
+// balances the uneven causal items), or by striding over the list when no
+// counter is given. Returns -1 when the list is exhausted.
+__device__ __forceinline__ int64_t next_item(const TcLaunch& L, int64_t& static_next, int64_t n_items,
+                                             int n_qtp, int nkb) {
+    while (true) {
+        int64_t it;
+        if (L.work_counter != nullptr) {
+            it = atomicAdd(L.work_counter, 1);
+        } else {
+            it = static_next;
+            static_next += gridDim.x;
+        }
+        if (it >= n_items) return -1;
+        const Item w = decode_item(L, it, n_qtp, nkb);
+        if (head_selected(L.sel, w.bh) && w.nblk > 0) return it;
+    }
+}
+
+// Consumers read the producer's item choices in order from a 4-slot ring.
+__device__ __forceinline__ bool take_item(TcBarriers* bars, uint32_t& ic, int64_t& it,
+                                          volatile int* abort_flag, uint64_t tmo, unsigned int* status) {
+    const uint32_t slot = ic & 3u;
+    if (!mbar_wait(smem_u32(&bars->item_full[slot]), (ic >> 2) & 1u, abort_flag, tmo, status)) return false;
+    it = static_cast<const volatile int64_t*>(bars->item_q)[slot];
+    mbar_arrive(smem_u32(&bars->item_empty[slot]));
+    ++ic;
+    return it >= 0;
+}
+
 template <int ELT, int DQK, int DV>
 __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_constant__ TcLaunch L) {
     using C = TcCfg<ELT, DQK, DV>;
     extern __shared__ uint8_t smem_raw[];
 
-    const int64_t BH = L.B * L.H;
     const int n_qt = ceil_div_i(L.Nq, 128);
     const int n_qtp = (n_qt + 1) / 2;
-    const int64_t lin = blockIdx.x;
-    const int64_t bh = lin % BH;
-    const int qtp = n_qtp - 1 - static_cast<int>(lin / BH);  // heavy (late) tiles first
-    if (!head_selected(L.sel, bh)) return;                    // whole CTA, before any sync
-    const int b = static_cast<int>(bh / L.H);
-    const int h = static_cast<int>(bh % L.H);
+    const int nkb = ceil_div_i(L.Nk, 128);
+    const int64_t n_items = L.B * L.H * n_qtp;
 
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = base;
-    uint8_t* sKV = base + 2 * C::Q_BYTES;
+    uint8_t* sQ = base;                        // [2 buffers][2 tiles][Q_BYTES]
+    uint8_t* sKV = base + 2 * C::QBUF_BYTES;   // [NSTAGE][STAGE_BYTES]
     TcBarriers* bars = reinterpret_cast<TcBarriers*>(sKV + C::NSTAGE * C::STAGE_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    // Key blocks each query tile needs.
-    const int nkb = ceil_div_i(L.Nk, 128);
-    int n_t[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const int64_t r0 = (static_cast<int64_t>(qtp) * 2 + t) * 128;
-        if (r0 >= L.Nq) {
-            n_t[t] = 0;
-        } else if (L.causal) {
-            const int64_t r_last = (r0 + 127 < L.Nq - 1) ? r0 + 127 : L.Nq - 1;
-            const int need = static_cast<int>(r_last / 128) + 1;
-            n_t[t] = need < nkb ? need : nkb;
-        } else {
-            n_t[t] = nkb;
-        }
-    }
-    const int nblk = n_t[0] > n_t[1] ? n_t[0] : n_t[1];
-
     if (threadIdx.x == 0) {
-        mbar_init(smem_u32(&bars->q_full), 1);
-        for (int t = 0; t < 2; ++t) {
-            mbar_init(smem_u32(&bars->s_full[t]), 1);
-            mbar_init(smem_u32(&bars->p_full[t]), 128);
-            mbar_init(smem_u32(&bars->o_full[t]), 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&bars->q_full[i]), 1);
+            mbar_init(smem_u32(&bars->q_empty[i]), 1);
+            mbar_init(smem_u32(&bars->s_full[i]), 1);
+            mbar_init(smem_u32(&bars->p_full[i]), 128);
+            mbar_init(smem_u32(&bars->o_full[i]), 1);
         }
         mbar_init(smem_u32(&bars->teardown), 1);
+        for (int i = 0; i < 4; ++i) {
+            mbar_init(smem_u32(&bars->item_full[i]), 1);
+            mbar_init(smem_u32(&bars->item_empty[i]), kItemConsumers);
+        }
         for (int s = 0; s < C::NSTAGE; ++s) {
             mbar_init(smem_u32(&bars->kv_full[s]), 1);
             mbar_init(smem_u32(&bars->kv_empty[s]), 1);
@@ -164,51 +244,76 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
     volatile int* abort_flag = &bars->abort_flag;
     const uint64_t tmo = L.timeout_ns;
 
-    if (warp == 8) {
+    if (warp >= 8) {
+      regs_decrease<kOtherRegs>();
+      if (warp == 8) {
         // ---------------- TMA producer ----------------
-        if (lane == 0 && nblk > 0) {
+        if (lane == 0) {
             tma_prefetch_desc(&L.tq);
             tma_prefetch_desc(&L.tk);
             tma_prefetch_desc(&L.tv);
-            const uint32_t qbar = smem_u32(&bars->q_full);
-            mbar_arrive_expect_tx(qbar, 2 * C::Q_BYTES);
-            for (int t = 0; t < 2; ++t)
-                for (int a = 0; a < C::QK_ATOMS; ++a)
-                    tma_load_4d(smem_u32(sQ + t * C::Q_BYTES + a * C::BOX), &L.tq, qbar,
-                                a * C::ATOM_COLS, (qtp * 2 + t) * 128, h, b);
-            for (int j = 0; j < nblk; ++j) {
-                for (int half = 0; half < 2; ++half) {
-                    const int idx = 2 * j + half;
-                    const int st = idx % C::NSTAGE;
-                    const uint32_t ph = (idx / C::NSTAGE) & 1;
-                    if (!mbar_wait(smem_u32(&bars->kv_empty[st]), ph ^ 1u, abort_flag, tmo, L.status))
-                        break;
-                    const uint32_t fbar = smem_u32(&bars->kv_full[st]);
-                    uint8_t* dst = sKV + st * C::STAGE_BYTES;
-                    if (half == 0) {
-                        mbar_arrive_expect_tx(fbar, C::K_BYTES);
-                        for (int a = 0; a < C::QK_ATOMS; ++a)
-                            tma_load_4d(smem_u32(dst + a * C::BOX), &L.tk, fbar, a * C::ATOM_COLS,
-                                        j * 128, h, b);
-                    } else {
-                        mbar_arrive_expect_tx(fbar, C::V_BYTES);
-                        for (int a = 0; a < C::V_ATOMS; ++a)
-                            tma_load_4d(smem_u32(dst + a * C::BOX), &L.tv, fbar, a * C::ATOM_COLS,
-                                        j * 128, h, b);
+            uint32_t qi = 0;   // items loaded by this CTA
+            uint32_t kvi = 0;  // ring slots filled
+            uint32_t ic = 0;   // items broadcast
+            int64_t static_next = blockIdx.x;
+            bool ok = true;
+            while (ok) {
+                const int64_t it = next_item(L, static_next, n_items, n_qtp, nkb);
+                const uint32_t slot = ic & 3u;
+                ok = mbar_wait(smem_u32(&bars->item_empty[slot]), ((ic >> 2) & 1u) ^ 1u, abort_flag, tmo,
+                               L.status);
+                if (!ok) break;
+                static_cast<volatile int64_t*>(bars->item_q)[slot] = it;
+                mbar_arrive(smem_u32(&bars->item_full[slot]));
+                ++ic;
+                if (it < 0) break;
+                const Item w = decode_item(L, it, n_qtp, nkb);
+                const uint32_t qb = qi & 1u;
+                ok = mbar_wait(smem_u32(&bars->q_empty[qb]), ((qi >> 1) & 1u) ^ 1u, abort_flag, tmo, L.status);
+                if (!ok) break;
+                const uint32_t qbar = smem_u32(&bars->q_full[qb]);
+                mbar_arrive_expect_tx(qbar, C::QBUF_BYTES);
+                for (int t = 0; t < 2; ++t)
+                    for (int a = 0; a < C::QK_ATOMS; ++a)
+                        tma_load_4d(smem_u32(sQ + qb * C::QBUF_BYTES + t * C::Q_BYTES + a * C::BOX), &L.tq,
+                                    qbar, a * C::ATOM_COLS, (w.qtp * 2 + t) * 128, w.h, w.b);
+                ++qi;
+                for (int j = 0; ok && j < w.nblk; ++j) {
+                    for (int half = 0; half < 2; ++half) {
+                        const uint32_t st = kvi % C::NSTAGE;
+                        const uint32_t ph = (kvi / C::NSTAGE) & 1u;
+                        ok = mbar_wait(smem_u32(&bars->kv_empty[st]), ph ^ 1u, abort_flag, tmo, L.status);
+                        if (!ok) break;
+                        const uint32_t fbar = smem_u32(&bars->kv_full[st]);
+                        uint8_t* dst = sKV + st * C::STAGE_BYTES;
+                        if (half == 0) {
+                            mbar_arrive_expect_tx(fbar, C::K_BYTES);
+                            for (int a = 0; a < C::QK_ATOMS; ++a)
+                                tma_load_4d(smem_u32(dst + a * C::BOX), &L.tk, fbar, a * C::ATOM_COLS,
+                                            j * 128, w.h, w.b);
+                        } else {
+                            mbar_arrive_expect_tx(fbar, C::V_BYTES);
+                            for (int a = 0; a < C::V_ATOMS; ++a)
+                                tma_load_4d(smem_u32(dst + a * C::BOX), &L.tv, fbar, a * C::ATOM_COLS,
+                                            j * 128, w.h, w.b);
+                        }
+                        ++kvi;
                     }
                 }
-                if (*abort_flag) break;
             }
         }
         __syncwarp();
     } else if (warp == 9) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0 && nblk > 0) {
+        if (lane == 0) {
             const uint32_t sQa = smem_u32(sQ);
             const uint32_t sKVa = smem_u32(sKV);
-            bool ok = mbar_wait(smem_u32(&bars->q_full), 0, abort_flag, tmo, L.status);
-            auto issue_s = [&](int t, int stage) {
-                const uint32_t q0 = sQa + t * C::Q_BYTES;
+            uint32_t qi = 0, kvi = 0, ic = 0;
+            uint32_t pc[2] = {0u, 0u};  // P blocks consumed per tile
+            bool ok = true;
+            int64_t it;
+            auto issue_s = [&](int t, uint32_t qbuf, uint32_t stage) {
+                const uint32_t q0 = sQa + qbuf * C::QBUF_BYTES + t * C::Q_BYTES;
                 const uint32_t k0 = sKVa + stage * C::STAGE_BYTES;
 #pragma unroll
                 for (int ks = 0; ks < DQK / C::MMA_K; ++ks) {
@@ -220,7 +325,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 }
                 tc_commit(smem_u32(&bars->s_full[t]));
             };
-            auto issue_pv = [&](int t, int stage, bool first) {
+            auto issue_pv = [&](int t, uint32_t stage, bool first) {
                 const uint32_t v0 = sKVa + stage * C::STAGE_BYTES;
 #pragma unroll
                 for (int ks = 0; ks < C::BN / C::MMA_K; ++ks) {
@@ -230,191 +335,259 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                                       (!first || ks > 0) ? 1u : 0u);
                 }
             };
-            if (ok) {
+            while (ok && take_item(bars, ic, it, abort_flag, tmo, L.status)) {
+                const Item w = decode_item(L, it, n_qtp, nkb);
+                const uint32_t qb = qi & 1u;
+                ok = mbar_wait(smem_u32(&bars->q_full[qb]), (qi >> 1) & 1u, abort_flag, tmo, L.status);
+                if (!ok) break;
                 // K_0 and the first score blocks.
-                ok = mbar_wait(smem_u32(&bars->kv_full[0]), 0, abort_flag, tmo, L.status);
-                if (ok) {
+                {
+                    const uint32_t st = kvi % C::NSTAGE;
+                    ok = mbar_wait(smem_u32(&bars->kv_full[st]), (kvi / C::NSTAGE) & 1u, abort_flag, tmo, L.status);
+                    if (!ok) break;
                     tc_fence_after();
                     for (int t = 0; t < 2; ++t)
-                        if (n_t[t] > 0) issue_s(t, 0);
-                    tc_commit(smem_u32(&bars->kv_empty[0]));
+                        if (w.n_t[t] > 0) issue_s(t, qb, st);
+                    tc_commit(smem_u32(&bars->kv_empty[st]));
                 }
-            }
-            for (int j = 0; ok && j < nblk; ++j) {
-                const int iv = 2 * j + 1;
-                const int sv = iv % C::NSTAGE;
-                ok = mbar_wait(smem_u32(&bars->kv_full[sv]), (iv / C::NSTAGE) & 1, abort_flag, tmo,
-                               L.status);
-                if (!ok) break;
-                tc_fence_after();
-                const int ik = 2 * j + 2;
-                const int sk = ik % C::NSTAGE;
-                bool k_ready = false;
-                for (int t = 0; t < 2 && ok; ++t) {
-                    if (j < n_t[t]) {
-                        ok = mbar_wait(smem_u32(&bars->p_full[t]), j & 1, abort_flag, tmo, L.status);
+                for (int j = 0; ok && j < w.nblk; ++j) {
+                    const uint32_t iv = kvi + 2 * j + 1;
+                    const uint32_t sv = iv % C::NSTAGE;
+                    ok = mbar_wait(smem_u32(&bars->kv_full[sv]), (iv / C::NSTAGE) & 1u, abort_flag, tmo,
+                                   L.status);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t ik = kvi + 2 * j + 2;
+                    const uint32_t sk = ik % C::NSTAGE;
+                    bool k_ready = false;
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
                         if (!ok) break;
-                        tc_fence_after();
-                        issue_pv(t, sv, j == 0);
-                        if (j == n_t[t] - 1) tc_commit(smem_u32(&bars->o_full[t]));
-                    }
-                    if (j + 1 < n_t[t]) {
-                        if (!k_ready) {
-                            ok = mbar_wait(smem_u32(&bars->kv_full[sk]), (ik / C::NSTAGE) & 1,
-                                           abort_flag, tmo, L.status);
+                        if (j < w.n_t[t]) {
+                            ok = mbar_wait(smem_u32(&bars->p_full[t]), pc[t] & 1u, abort_flag, tmo, L.status);
                             if (!ok) break;
+                            ++pc[t];
                             tc_fence_after();
-                            k_ready = true;
+                            issue_pv(t, sv, j == 0);
+                            if (j == w.n_t[t] - 1) tc_commit(smem_u32(&bars->o_full[t]));
                         }
-                        issue_s(t, sk);
+                        if (j + 1 < w.n_t[t]) {
+                            if (!k_ready) {
+                                ok = mbar_wait(smem_u32(&bars->kv_full[sk]), (ik / C::NSTAGE) & 1u,
+                                               abort_flag, tmo, L.status);
+                                if (!ok) break;
+                                tc_fence_after();
+                                k_ready = true;
+                            }
+                            issue_s(t, qb, sk);
+                        }
                     }
+                    tc_commit(smem_u32(&bars->kv_empty[sv]));
+                    if (k_ready) tc_commit(smem_u32(&bars->kv_empty[sk]));
                 }
-                tc_commit(smem_u32(&bars->kv_empty[sv]));
-                if (k_ready) tc_commit(smem_u32(&bars->kv_empty[sk]));
+                // Every S product of this item is issued: the Q buffer frees
+                // when they complete.
+                tc_commit(smem_u32(&bars->q_empty[qb]));
+                kvi += 2 * w.nblk;
+                ++qi;
             }
             // Everything issued so far completes before the CTA frees TMEM.
             tc_commit(smem_u32(&bars->teardown));
             teardown_wait(smem_u32(&bars->teardown), 0, tmo, L.status);
         }
         __syncwarp();
+      }
     } else {
+        regs_increase<kSoftmaxRegs>();
         // ---------------- softmax warpgroups ----------------
         const int t = warp >> 2;
         const int row = (warp & 3) * 32 + lane;  // TMEM lane == row of the tile
-        const int64_t qrow = (static_cast<int64_t>(qtp) * 2 + t) * 128 + row;
         const uint32_t lane_bits = static_cast<uint32_t>((warp & 3) * 32) << 16;
         const uint32_t tS = tmem + lane_bits + t * 128;
         const uint32_t tO = tmem + lane_bits + 256 + t * DV;
-        const int nt = n_t[t];
-        const int64_t tile_r0 = (static_cast<int64_t>(qtp) * 2 + t) * 128;
-        float sq = 1.f;
-        if constexpr (ELT == 2) {
-            if (nt > 0) sq = L.q_scale[bh * L.nt_q + (qtp * 2 + t)];  // tile exists
-        }
-        float m_run = -INFINITY;
-        float l_run = 0.f;
+        uint32_t sc = 0;  // S blocks consumed by this tile
+        uint32_t oc = 0;  // items finished by this tile
         bool ok = true;
-        for (int j = 0; j < nt; ++j) {
-            ok = mbar_wait(smem_u32(&bars->s_full[t]), j & 1, abort_flag, tmo, L.status);
-            if (!ok) break;
-            tc_fence_after();
-            float s[128];
-            {
-                uint32_t r[32];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    tmem_ld32(tS + c * 32, r);
+        uint32_t ic = 0;
+        int64_t it;
+        while (ok && take_item(bars, ic, it, abort_flag, tmo, L.status)) {
+            const Item w = decode_item(L, it, n_qtp, nkb);
+            const int nt = w.n_t[t];
+            if (nt == 0) continue;
+            const int tile_r0 = (w.qtp * 2 + t) * 128;
+            const int qrow = tile_r0 + row;
+            const int Nk = static_cast<int>(L.Nk);
+            float sq = 1.f;
+            if constexpr (ELT == 2) sq = L.q_scale[w.bh * L.nt_q + (w.qtp * 2 + t)];
+            float m_run = -INFINITY;
+            float l_run = 0.f;
+            for (int j = 0; j < nt; ++j) {
+                ok = mbar_wait(smem_u32(&bars->s_full[t]), sc & 1u, abort_flag, tmo, L.status);
+                if (!ok) break;
+                ++sc;
+                tc_fence_after();
+                float s[128];
+                {
+                    uint32_t r0[32], r1[32], r2[32], r3[32];
+                    tmem_ld32(tS + 0, r0);
+                    tmem_ld32(tS + 32, r1);
+                    tmem_ld32(tS + 64, r2);
+                    tmem_ld32(tS + 96, r3);
                     tmem_ld_wait();
-                    reg_fence32(r);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-                }
-            }
-            float sl2 = L.scale_log2;
-            if constexpr (ELT == 2) sl2 *= sq * L.k_scale[bh * L.nt_k + j];
-            const int64_t kv0 = static_cast<int64_t>(j) * 128;
-            const bool edge = (kv0 + 128 > L.Nk) || (L.causal && kv0 + 127 > tile_r0);
-            if (edge) {
-#pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const int64_t kv = kv0 + c;
-                    if (kv >= L.Nk || (L.causal && kv > qrow)) s[c] = -INFINITY;
-                }
-            }
-            if (L.mask.data != nullptr && qrow < L.Nq) {
-                // logits are s * scale + m; in raw-score units that is s + m / scale.
-                const float inv_scale = 1.f / (sl2 * 0.69314718056f);
-                const int64_t mb = b * L.mask.s[0] + h * L.mask.s[1] + qrow * L.mask.s[2];
-#pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const int64_t kv = kv0 + c;
-                    if (kv < L.Nk) {
-                        const float mv = load_as_f32(L.mask.data, mb + kv * L.mask.s[3], L.mask.dtype);
-                        if (L.mask.dtype == ADA_BOOL) {
-                            if (mv == 0.f) s[c] = -INFINITY;
-                        } else {
-                            s[c] += round_to(mv, L.round_dtype) * inv_scale;
-                        }
-                    }
-                }
-            }
-            float mx[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) mx[i] = s[i];
-#pragma unroll
-            for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
-            const float m_blk = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                      fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-            const float m_cand = m_blk * sl2;
-            float m_new = m_run;
-            if constexpr (ELT == 2) {
-                m_new = fmaxf(m_run, m_cand);
-            } else {
-                // Keep a stale maximum until it falls 8 (log2 units) behind:
-                // P stays <= 256, exact in 16-bit, and O is rescaled rarely.
-                if (m_cand > m_run + 8.f) m_new = m_cand;
-            }
-            const float alpha = (m_new == m_run) ? 1.f : fast_exp2(m_run - m_new);
-            const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
-            float ls[4] = {0.f, 0.f, 0.f, 0.f};
-            {
-                constexpr int NP = C::P_COLS / 32;  // 32-column chunks of P
-                uint32_t pr[32];
-#pragma unroll
-                for (int chunk = 0; chunk < NP; ++chunk) {
+                    reg_fence32(r0);
+                    reg_fence32(r1);
+                    reg_fence32(r2);
+                    reg_fence32(r3);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        if constexpr (ELT == 2) {
-                            const int c = chunk * 128 + i * 4;
-                            float p0 = fast_exp2(fmaf(s[c + 0], sl2, neg_m));
-                            float p1 = fast_exp2(fmaf(s[c + 1], sl2, neg_m));
-                            float p2 = fast_exp2(fmaf(s[c + 2], sl2, neg_m));
-                            float p3 = fast_exp2(fmaf(s[c + 3], sl2, neg_m));
-                            ls[0] += p0;
-                            ls[1] += p1;
-                            ls[2] += p2;
-                            ls[3] += p3;
-                            pr[i] = pack_e4m3x4(p0 * 448.f, p1 * 448.f, p2 * 448.f, p3 * 448.f);
-                        } else {
-                            const int c = chunk * 64 + i * 2;
-                            float p0 = fast_exp2(fmaf(s[c + 0], sl2, neg_m));
-                            float p1 = fast_exp2(fmaf(s[c + 1], sl2, neg_m));
-                            ls[i & 1] += p0;
-                            ls[2 + (i & 1)] += p1;
-                            pr[i] = (ELT == 1) ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+                        s[i] = __uint_as_float(r0[i]);
+                        s[32 + i] = __uint_as_float(r1[i]);
+                        s[64 + i] = __uint_as_float(r2[i]);
+                        s[96 + i] = __uint_as_float(r3[i]);
+                    }
+                }
+                float sl2 = L.scale_log2;
+                if constexpr (ELT == 2) sl2 *= sq * L.k_scale[w.bh * L.nt_k + j];
+                const int kv0 = j * 128;
+                const bool edge = (kv0 + 128 > Nk) || (L.causal && kv0 + 127 > tile_r0);
+                if (edge) {
+                    const int lim_k = Nk - kv0;                                   // keys >= Nk
+                    const int lim_c = L.causal ? (qrow - kv0 + 1) : 128;          // keys > qrow
+                    const int lim = lim_k < lim_c ? lim_k : lim_c;
+#pragma unroll
+                    for (int c = 0; c < 128; ++c)
+                        if (c >= lim) s[c] = -INFINITY;
+                }
+                if (L.mask.data != nullptr && qrow < L.Nq) {
+                    // logits are s * scale + m; in raw-score units that is s + m / scale.
+                    const float inv_scale = 1.f / (sl2 * 0.69314718056f);
+                    const int64_t mb = w.b * L.mask.s[0] + w.h * L.mask.s[1] + qrow * L.mask.s[2];
+#pragma unroll
+                    for (int c = 0; c < 128; ++c) {
+                        const int kv = kv0 + c;
+                        if (kv < Nk) {
+                            const float mv = load_as_f32(L.mask.data, mb + kv * L.mask.s[3], L.mask.dtype);
+                            if (L.mask.dtype == ADA_BOOL) {
+                                if (mv == 0.f) s[c] = -INFINITY;
+                            } else {
+                                s[c] += round_to(mv, L.round_dtype) * inv_scale;
+                            }
                         }
                     }
-                    tmem_st32(tS + chunk * 32, pr);
                 }
-            }
-            l_run = l_run * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                uint32_t r[32];
+                // Row maximum: 8 chains over s[0..127] (two new values per
+                // three-input max, the last eight with a plain max).
+                float mx[8];
 #pragma unroll
-                for (int c = 0; c < DV / 32; ++c) {
-                    tmem_ld32(tO + c * 32, r);
-                    tmem_ld_wait();
-                    reg_fence32(r);
+                for (int i = 0; i < 8; ++i) mx[i] = s[i];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                    tmem_st32(tO + c * 32, r);
+                for (int c = 8; c + 16 <= 128; c += 16)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) mx[i] = max3f(mx[i], s[c + i], s[c + 8 + i]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], s[120 + i]);
+                const float m_blk = max3f(max3f(mx[0], mx[1], mx[2]), max3f(mx[3], mx[4], mx[5]),
+                                          fmaxf(mx[6], mx[7]));
+                const float m_cand = m_blk * sl2;
+                float m_new = m_run;
+                if constexpr (ELT == 2) {
+                    m_new = fmaxf(m_run, m_cand);
+                } else {
+                    // Keep a stale maximum until it falls 8 (log2 units) behind:
+                    // P stays <= 256, exact in 16-bit, and O is rescaled rarely.
+                    if (m_cand > m_run + 8.f) m_new = m_cand;
                 }
+                const float alpha = (m_new == m_run) ? 1.f : fast_exp2(m_run - m_new);
+                const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
+                const uint64_t sl2p = f2_pack(sl2, sl2);
+                const uint64_t nmp = f2_pack(neg_m, neg_m);
+                uint64_t ls0 = f2_pack(0.f, 0.f), ls1 = ls0;
+                // P = 2^(s * scale * log2(e) - m), written over the S columns.
+                // Without a user mask, kPolyPairs of every 8 pairs take the
+                // polynomial exponential on the FMA pipe so the MUFU unit is
+                // not the limit (masked keys there give ~2e-38, not 0).
+                auto compute_p = [&](auto poly_tag) {
+                    constexpr bool kPoly = decltype(poly_tag)::value;
+                    constexpr int NP = C::P_COLS / 32;  // 32-column chunks of P
+                    uint32_t pr[32];
+#pragma unroll
+                    for (int chunk = 0; chunk < NP; ++chunk) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if constexpr (ELT == 2) {
+                                const int c = chunk * 128 + i * 4;
+                                float p0, p1, p2, p3;
+                                f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2p, nmp), p0, p1);
+                                f2_unpack(f2_fma(f2_pack(s[c + 2], s[c + 3]), sl2p, nmp), p2, p3);
+                                p0 = fast_exp2(p0);
+                                p1 = fast_exp2(p1);
+                                p2 = fast_exp2(p2);
+                                p3 = fast_exp2(p3);
+                                ls0 = f2_add(ls0, f2_pack(p0, p1));
+                                ls1 = f2_add(ls1, f2_pack(p2, p3));
+                                pr[i] = pack_e4m3x4(p0 * 448.f, p1 * 448.f, p2 * 448.f, p3 * 448.f);
+                            } else {
+                                const int c = chunk * 64 + i * 2;
+                                float p0, p1;
+                                f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2p, nmp), p0, p1);
+                                if (kPoly && (i % 8) < kPolyPairs) {
+                                    exp2_poly2(p0, p1, p0, p1);
+                                } else {
+                                    p0 = fast_exp2(p0);
+                                    p1 = fast_exp2(p1);
+                                }
+                                if (i & 1)
+                                    ls1 = f2_add(ls1, f2_pack(p0, p1));
+                                else
+                                    ls0 = f2_add(ls0, f2_pack(p0, p1));
+                                pr[i] = (ELT == 1) ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+                            }
+                        }
+                        tmem_st32(tS + chunk * 32, pr);
+                    }
+                };
+                if (L.mask.data == nullptr)
+                    compute_p(std::integral_constant<bool, true>{});
+                else
+                    compute_p(std::integral_constant<bool, false>{});
+                float la, lb, lc, ld;
+                f2_unpack(ls0, la, lb);
+                f2_unpack(ls1, lc, ld);
+                l_run = l_run * alpha + ((la + lb) + (lc + ld));
+                if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                    const uint64_t ap = f2_pack(alpha, alpha);
+                    uint32_t r[32];
+#pragma unroll
+                    for (int c = 0; c < DV / 32; ++c) {
+                        tmem_ld32(tO + c * 32, r);
+                        tmem_ld_wait();
+                        reg_fence32(r);
+#pragma unroll
+                        for (int i = 0; i < 32; i += 2) {
+                            float x0, x1;
+                            f2_unpack(f2_mul(f2_pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), ap), x0, x1);
+                            r[i] = __float_as_uint(x0);
+                            r[i + 1] = __float_as_uint(x1);
+                        }
+                        tmem_st32(tO + c * 32, r);
+                    }
+                }
+                m_run = m_new;
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(smem_u32(&bars->p_full[t]));
             }
-            m_run = m_new;
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(smem_u32(&bars->p_full[t]));
-        }
-        if (nt > 0 && ok) {
-            ok = mbar_wait(smem_u32(&bars->o_full[t]), 0, abort_flag, tmo, L.status);
-        }
-        if (nt > 0 && ok) {
+            if (!ok) break;
+            ok = mbar_wait(smem_u32(&bars->o_full[t]), oc & 1u, abort_flag, tmo, L.status);
+            if (!ok) break;
+            ++oc;
             tc_fence_after();
+            // ---- epilogue: O / l, rounded like the reference's result, stored ----
             float post = 1.f / l_run;
-            if constexpr (ELT == 2) post *= L.v_scale[bh] * (1.f / 448.f);
+            if constexpr (ELT == 2) post *= L.v_scale[w.bh] * (1.f / 448.f);
             const bool row_ok = qrow < L.Nq;
             uint8_t* orow = reinterpret_cast<uint8_t*>(L.out);
-            const int64_t obase = b * L.os[0] + h * L.os[1] + qrow * L.os[2];
+            const int64_t obase = w.b * L.os[0] + w.h * L.os[1] + static_cast<int64_t>(qrow) * L.os[2];
             uint32_t r[32];
 #pragma unroll
             for (int c = 0; c < DV / 32; ++c) {
@@ -436,13 +609,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                             uint4* dst = reinterpret_cast<uint4*>(orow + (obase + col0) * 2);
 #pragma unroll
                             for (int i = 0; i < 4; ++i) {
-                                uint32_t w[4];
+                                uint32_t wv[4];
 #pragma unroll
                                 for (int k2 = 0; k2 < 4; ++k2) {
                                     const float lo = o[8 * i + 2 * k2], hi = o[8 * i + 2 * k2 + 1];
-                                    w[k2] = (L.out_dtype == ADA_BF16) ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+                                    wv[k2] = (L.out_dtype == ADA_BF16) ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
                                 }
-                                dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                                dst[i] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                             }
                         }
                     } else {
@@ -463,6 +636,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
     }
 }
 
+
 template <int ELT, int DQK, int DV>
 int launch_variant(const TcLaunch& L, cudaStream_t stream) {
     using C = TcCfg<ELT, DQK, DV>;
@@ -470,11 +644,21 @@ int launch_variant(const TcLaunch& L, cudaStream_t stream) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
         cudaSuccess)
         return ADA_ERR_LAUNCH;
+    // The register hand-over inside the kernel needs the full launch pool; a
+    // build that allocated fewer registers would wait forever in setmaxnreg.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kLaunchRegs)
+        return ADA_ERR_UNSUPPORTED;
     const int64_t n_qt = (L.Nq + 127) / 128;
     const int64_t n_qtp = (n_qt + 1) / 2;
-    const int64_t grid = n_qtp * L.B * L.H;
-    if (grid <= 0) return ADA_OK;
-    if (grid > 0x7fffffffLL) return ADA_ERR_UNSUPPORTED;
+    const int64_t items = n_qtp * L.B * L.H;
+    if (items <= 0) return ADA_OK;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ADA_ERR_LAUNCH;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        return ADA_ERR_LAUNCH;
+    const int64_t grid = items < sms ? items : sms;
     kern<<<static_cast<unsigned>(grid), kThreadsTc, C::SMEM_BYTES, stream>>>(L);
     return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
