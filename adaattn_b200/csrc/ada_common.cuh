@@ -312,31 +312,6 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
 
 __device__ __forceinline__ uint64_t f2_splat(float v) { return f2_pack(v, v); }
 
-// 2^x for a pair of inputs on the FMA and integer pipes instead of the MUFU
-// unit (which caps the softmax at 16 exponentials per clock per SM).
-// Method: x = j + f with j = round(x) (added to 1.5 * 2^23 so j lands in the
-// low mantissa bits) and f in [-0.5, 0.5]; 2^f by a cubic fitted here for
-// minimal maximum relative error on [-0.5, 0.5] (Lawson-weighted least
-// squares; max relative error 7.6e-5); 2^j by adding j to the exponent
-// field. Inputs are clamped to [-125, +inf): results below 2^-125 come out
-// as about 2e-38 rather than 0, which callers only use where that is
-// negligible (no fully masked rows). Valid for x <= 127.
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-    const uint64_t t = f2_add(x, f2_splat(kMagic));
-    const uint64_t jf = f2_add(t, f2_splat(-kMagic));
-    const uint64_t fr = f2_fma(jf, f2_splat(-1.f), x);
-    uint64_t p = f2_fma(f2_splat(0.055170251320173225f), fr, f2_splat(0.24260790504365293f));
-    p = f2_fma(p, fr, f2_splat(0.6932609265307287f));
-    p = f2_fma(p, fr, f2_splat(0.9999282806662734f));
-    float t0, t1, p0, p1;
-    f2_unpack(t, t0, t1);
-    f2_unpack(p, p0, p1);
-    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -3,13 +3,16 @@
 // Persistent CTAs (one per SM) walk a list of work items; an item is two
 // 128-row query tiles of one (b, h). Items are ordered head-major (the tiles
 // of one head run side by side, so its K and V stream from L2) and, within a
-// head, heavy-first (late tiles have more keys under causal masking); CTA c
-// takes items c, c + grid, c + 2*grid, ...
+// head, heavy-first (late tiles have more keys under causal masking). The
+// producer warp of each CTA takes the next item from a shared counter
+// (dynamic scheduling balances the uneven causal items) and broadcasts it to
+// the other roles through a small shared-memory ring; without a counter the
+// CTAs stride over the list.
 //
 // Per item, 128-key blocks of K and V stream through a shared-memory ring
 // filled by TMA. S = Q K^T (SS) and O += P V (TS: P read from tensor memory)
 // run as tcgen05 MMAs with fp32 accumulators in TMEM; the score block never
-// leaves the SM. Warp roles (320 threads):
+// leaves the SM. Warp roles (384 threads, three warpgroups):
 //   warps 0-3 / 4-7  softmax for query tile 0 / 1: read S from TMEM (one row
 //                    per thread), online softmax in registers, write P (16-bit
 //                    or E4M3) over the S columns, rescale O when the running
@@ -17,6 +20,8 @@
 //   warp 8           TMA producer (Q tiles per item, double buffered; then
 //                    K_j, V_j through the ring).
 //   warp 9           TMEM allocation and the single-thread MMA issuer.
+//   warps 10-11      idle (they complete the third warpgroup, which hands
+//                    its registers to the softmax warpgroups).
 // The two query tiles ping-pong: while one tile's softmax runs, the tensor
 // core works on the other tile's products. Across items the producer and the
 // MMA issuer run ahead, so the next item's first products overlap this item's
@@ -45,12 +50,6 @@ constexpr int kOtherRegs = 88;
 constexpr int kItemConsumers = 1 + 256;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreadsTc * kLaunchRegs,
               "register split exceeds the launch pool");
-// Pairs of scores (of every 8 pairs) whose exponential runs as a polynomial
-// on the FMA pipe; the rest use MUFU ex2.
-#ifndef ADA_EXP2_POLY_PAIRS
-#define ADA_EXP2_POLY_PAIRS 0
-#endif
-constexpr int kPolyPairs = ADA_EXP2_POLY_PAIRS;
 // Dynamic shared memory budget: 227 KB per CTA minus alignment slack and the
 // barrier block.
 constexpr int kSmemBudget = 232448 - 1024 - 512;
@@ -503,11 +502,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 const uint64_t nmp = f2_pack(neg_m, neg_m);
                 uint64_t ls0 = f2_pack(0.f, 0.f), ls1 = ls0;
                 // P = 2^(s * scale * log2(e) - m), written over the S columns.
-                // Without a user mask, kPolyPairs of every 8 pairs take the
-                // polynomial exponential on the FMA pipe so the MUFU unit is
-                // not the limit (masked keys there give ~2e-38, not 0).
-                auto compute_p = [&](auto poly_tag) {
-                    constexpr bool kPoly = decltype(poly_tag)::value;
+                {
                     constexpr int NP = C::P_COLS / 32;  // 32-column chunks of P
                     uint32_t pr[32];
 #pragma unroll
@@ -530,12 +525,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                                 const int c = chunk * 64 + i * 2;
                                 float p0, p1;
                                 f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2p, nmp), p0, p1);
-                                if (kPoly && (i % 8) < kPolyPairs) {
-                                    exp2_poly2(p0, p1, p0, p1);
-                                } else {
-                                    p0 = fast_exp2(p0);
-                                    p1 = fast_exp2(p1);
-                                }
+                                p0 = fast_exp2(p0);
+                                p1 = fast_exp2(p1);
                                 if (i & 1)
                                     ls1 = f2_add(ls1, f2_pack(p0, p1));
                                 else
@@ -545,11 +536,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                         }
                         tmem_st32(tS + chunk * 32, pr);
                     }
-                };
-                if (L.mask.data == nullptr)
-                    compute_p(std::integral_constant<bool, true>{});
-                else
-                    compute_p(std::integral_constant<bool, false>{});
+                }
                 float la, lb, lc, ld;
                 f2_unpack(ls0, la, lb);
                 f2_unpack(ls1, lc, ld);
