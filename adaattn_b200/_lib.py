@@ -65,6 +65,8 @@ _SIGNATURES = {
     "ada_analyze_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "ada_analyze": (c_int32, [_T, _T, POINTER(AdaAnalyzeParams), c_void_p, c_void_p,
                               c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ada_analyze_noalloc": (c_int32, [_T, _T, POINTER(AdaAnalyzeParams), c_void_p, c_void_p,
+                                      c_void_p, c_void_p]),
     "ada_attn_fwd_workspace_bytes": (c_size_t, [_T, _T, _T, _T, c_void_p,
                                                POINTER(AdaFwdParams), c_int32, c_int32]),
     "ada_attn_fwd": (c_int32, [_T, _T, _T, _T, _T, c_void_p, POINTER(AdaFwdParams),

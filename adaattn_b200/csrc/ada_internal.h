@@ -34,6 +34,8 @@ int launch_effective_rank(const void* w, int dtype, int64_t groups, int64_t grou
 int launch_target_ranks(const float* eff, int64_t n, int64_t min_rank, int64_t max_rank, double thr,
                         int64_t* out, cudaStream_t stream);
 int launch_bounded_wait(uint64_t timeout_ns, unsigned int* status, cudaStream_t stream);
+// Sets the calling thread's ada_get_last_error message; returns `code`.
+int record_last_error(int code, const char* msg);
 
 // --- which heads a launch serves ---------------------------------------------
 // A head (b,h) is served when decisions == nullptr (static decision) or when

@@ -424,3 +424,129 @@ int launch_bounded_wait(uint64_t timeout_ns, unsigned int* status, cudaStream_t 
 }
 
 }  // namespace ada
+
+// ---------------------------------------------------------------------------
+// ada_analyze_noalloc: the analyzer without a caller-provided workspace.
+//
+// For callers that cannot call cudaMalloc -- for example code that must run
+// inside a fixed device-memory budget set aside at start-up, or a caller whose
+// memory allocator is not reachable from the place it runs the analyzer -- the
+// per-head scratch that ada_analyze takes from the workspace lives here in a
+// file-scope device array instead. Its size is fixed (kNoAllocMaxHeads floats,
+// 256 KB), so batch * heads is limited to kNoAllocMaxHeads; every GPU that
+// loads this library keeps the array until the process exits.
+//
+// Every call shares the one array: calls that overlap on the GPU (different
+// streams, or different host threads on one device) race on it and must be
+// ordered by the caller. Each call writes every scratch entry it reads
+// before reading it, so nothing has to be cleared between calls.
+//
+// The first call on a device resolves the array's device address there
+// (cudaGetSymbolAddress with that device current); make that first call
+// before any stream capture. Nothing here calls cudaMalloc, cudaFree or an
+// allocating library routine.
+// ---------------------------------------------------------------------------
+#include <cmath>
+#include <mutex>
+
+namespace ada {
+namespace {
+
+constexpr int64_t kNoAllocMaxHeads = 65536;
+static __device__ __align__(256) float g_noalloc_head_sum[kNoAllocMaxHeads];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+
+// Once per device, with that device current: the device address of the
+// array. In host code the array's name is only a host-side stand-in.
+int noalloc_scratch(float** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
+        return record_last_error(ADA_ERR_DEVICE, "ada_analyze_noalloc: no usable current device");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10)
+            return record_last_error(ADA_ERR_DEVICE, "ada_analyze_noalloc: device is not sm_100");
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_head_sum);
+        if (e != cudaSuccess || p == nullptr)
+            return record_last_error(ADA_ERR_CUDA, "ada_analyze_noalloc: cudaGetSymbolAddress failed");
+        g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return ADA_OK;
+}
+
+bool attn_view_ok(const AdaTensor* t) {
+    if (t == nullptr || t->data == nullptr || t->ndim != 4) return false;
+    if (t->dtype != ADA_F32 && t->dtype != ADA_F16 && t->dtype != ADA_BF16) return false;
+    for (int i = 0; i < 4; ++i)
+        if (t->shape[i] < 0) return false;
+    return true;
+}
+
+}  // namespace
+}  // namespace ada
+
+extern "C" int ada_analyze_noalloc(const AdaTensor* q, const AdaTensor* k, const AdaAnalyzeParams* params,
+                                   int32_t* decisions, float* head_stats, float* summary, void* stream) {
+    using namespace ada;
+    if (!attn_view_ok(q) || !attn_view_ok(k))
+        return record_last_error(ADA_ERR_INVALID, "ada_analyze_noalloc: q and k must be 4-D float views");
+    if (params == nullptr || decisions == nullptr || head_stats == nullptr || summary == nullptr)
+        return record_last_error(ADA_ERR_INVALID, "ada_analyze_noalloc: null argument");
+    if (q->dtype != k->dtype) return record_last_error(ADA_ERR_DTYPE, "ada_analyze_noalloc: q and k dtypes differ");
+    if (q->shape[0] != k->shape[0] || q->shape[1] != k->shape[1] || q->shape[3] != k->shape[3])
+        return record_last_error(ADA_ERR_SHAPE, "ada_analyze_noalloc: q and k shapes disagree");
+    const int64_t B = q->shape[0], H = q->shape[1], Nq = q->shape[2], Nk = k->shape[2], D = q->shape[3];
+    if (B * H > kNoAllocMaxHeads)
+        return record_last_error(ADA_ERR_UNSUPPORTED,
+                                 "ada_analyze_noalloc: batch * heads exceeds the fixed scratch of 65536 "
+                                 "heads; use ada_analyze with a workspace");
+    if (D < 1 || D > 256) return record_last_error(ADA_ERR_UNSUPPORTED, "ada_analyze_noalloc: head dim outside [1, 256]");
+    if (Nq < 1 || Nk < 1) return record_last_error(ADA_ERR_SHAPE, "ada_analyze_noalloc: empty sequence");
+    if (params->default_precision < 0 || params->default_precision > 4)
+        return record_last_error(ADA_ERR_INVALID, "ada_analyze_noalloc: default precision out of range");
+    float* head_sum = nullptr;
+    const int rc = noalloc_scratch(&head_sum);
+    if (rc != ADA_OK) return rc;
+    if (B * H == 0) return ADA_OK;
+    const int stride = params->sample_stride > 1 ? params->sample_stride : 1;
+    const int64_t n_min = Nq < Nk ? Nq : Nk;
+    int64_t S = (n_min + stride - 1) / stride;
+    if (S > 64) S = 64;
+    AnalyzeLaunch L{};
+    L.q = q->data;
+    L.k = k->data;
+    L.dtype = q->dtype;
+    L.B = B;
+    L.H = H;
+    L.Nq = Nq;
+    L.Nk = Nk;
+    L.D = D;
+    for (int i = 0; i < 4; ++i) {
+        L.qs[i] = q->stride[i];
+        L.ks[i] = k->stride[i];
+    }
+    L.scale = params->scale;
+    L.eps = params->eps;
+    L.log_s = std::log(static_cast<double>(S));
+    L.S = static_cast<int>(S);
+    L.stride = stride;
+    L.head_stats = head_stats;
+    L.head_sum = head_sum;
+    L.decisions = decisions;
+    L.summary = summary;
+    L.rank_threshold = params->rank_threshold;
+    L.enable_rank = params->enable_adaptive_rank;
+    L.enable_prec = params->enable_adaptive_precision;
+    L.default_prec = params->default_precision;
+    L.allow_fp8 = params->allow_fp8;
+    L.granularity = params->granularity;
+    if (launch_analyze(L, static_cast<cudaStream_t>(stream)) != ADA_OK)
+        return record_last_error(ADA_ERR_LAUNCH, "ada_analyze_noalloc: launch failed");
+    return ADA_OK;
+}

@@ -345,6 +345,11 @@ void copy_strides(int64_t* dst, const AdaTensor* t) {
 }  // namespace
 }  // namespace ada
 
+namespace ada {
+// Lets entry points defined in other files report through ada_get_last_error.
+int record_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace ada
+
 using namespace ada;
 
 extern "C" {

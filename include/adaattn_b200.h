@@ -132,6 +132,21 @@ int         ada_analyze(const AdaTensor* q, const AdaTensor* k,
                         int32_t* decisions, float* head_stats, float* summary,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ada_analyze for callers that cannot call cudaMalloc (this entry point has no
+ * counterpart in the reference). Same inputs and outputs as ada_analyze, but
+ * the per-head scratch lives in a fixed device array inside the library
+ * instead of a caller workspace, so the call allocates nothing. Limit:
+ * batch * heads <= 65536 (the array is 256 KB and every device that loads the
+ * library holds it until the process exits); larger inputs return
+ * ADA_ERR_UNSUPPORTED. All calls share the array: calls that overlap on the
+ * GPU (other streams, other host threads on the same device) race on it and
+ * must be ordered by the caller. The first call on a device resolves the
+ * array's address on that device; make it before any stream capture. */
+int         ada_analyze_noalloc(const AdaTensor* q, const AdaTensor* k,
+                                const AdaAnalyzeParams* params,
+                                int32_t* decisions, float* head_stats, float* summary,
+                                void* stream);
+
 /* Adaptive attention core on [B,H,N,D]: every (b,h) slice takes the branch
  * (dense / low rank) and the precision its decision names. Replaces
  * AdaAttention._adaptive_attention_forward (adaattn.py:462-504) with

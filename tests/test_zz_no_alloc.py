@@ -1,0 +1,103 @@
+"""The analyzer entry point that allocates nothing (ada_analyze_noalloc).
+
+Some callers cannot call cudaMalloc: code that must stay inside a device-memory
+budget fixed at start-up, or code that runs the analyzer from a place where
+its memory allocator is not reachable. ada_analyze_noalloc serves them by
+keeping the per-head scratch that ada_analyze takes from a workspace in a
+fixed array inside the library.
+
+The test calls it through the C ABI twice in a row (the second call reuses
+the array the first one left behind) and checks both results against the
+workspace entry point, ada_analyze, on the same inputs: decisions identical,
+statistics identical (the same kernels run on the same data). It also checks
+the size limit is refused with a clear error. This file is collected last so
+that a run stopping at the first failure has run every other test first.
+"""
+
+import ctypes
+import math
+
+import pytest
+import torch
+
+from adaattn_b200 import PrecisionMode
+from adaattn_b200 import _lib
+from adaattn_b200.workloads import WORKLOADS, make_qkv
+
+pytestmark = pytest.mark.gpu
+
+LIMIT = 65536  # batch * heads the fixed scratch covers
+
+
+def _params(scale, granularity):
+    p = _lib.AdaAnalyzeParams()
+    p.rank_threshold = 0.95
+    p.scale = scale
+    p.eps = 1e-6
+    p.enable_adaptive_rank = 1
+    p.enable_adaptive_precision = 1
+    p.default_precision = PrecisionMode.FP16.code
+    p.allow_fp8 = 0
+    p.granularity = granularity
+    p.sample_stride = 1
+    return p
+
+
+def _outputs(b, h, dev):
+    return (torch.empty(b, h, 2, dtype=torch.int32, device=dev),
+            torch.empty(b, h, 4, dtype=torch.float32, device=dev),
+            torch.empty(_lib.SUMMARY_LEN, dtype=torch.float32, device=dev))
+
+
+def _with_workspace(lib, q, k, p, dev):
+    dec, st, sm = _outputs(q.shape[0], q.shape[1], dev)
+    ws = torch.empty(lib.ada_analyze_workspace_bytes(q.shape[0], q.shape[1]), dtype=torch.uint8,
+                     device=dev)
+    rc = lib.ada_analyze(_lib.tensor(q), _lib.tensor(k), p, dec.data_ptr(), st.data_ptr(),
+                         sm.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    _lib.check(rc, "ada_analyze")
+    return dec, st, sm
+
+
+def _no_alloc(lib, q, k, p, dev):
+    dec, st, sm = _outputs(q.shape[0], q.shape[1], dev)
+    rc = lib.ada_analyze_noalloc(_lib.tensor(q), _lib.tensor(k), p, dec.data_ptr(), st.data_ptr(),
+                                 sm.data_ptr(), _lib.stream_ptr(dev))
+    _lib.check(rc, "ada_analyze_noalloc")
+    return dec, st, sm
+
+
+@pytest.mark.parametrize("granularity", [0, 1])
+@pytest.mark.parametrize("workload,b,h,n", [("adaptive_mix", 2, 8, 512),
+                                            ("precision_mix", 4, 32, 256)])
+def test_no_alloc_matches_workspace_entry_point(workload, b, h, n, granularity, cuda_device):
+    lib = _lib.load()
+    w = WORKLOADS[workload].scaled(batch=b, heads=h, seq=n)
+    q, k, _ = make_qkv(w, seed=0, device=str(cuda_device))
+    p = _params(1.0 / math.sqrt(w.head_dim), granularity)
+    with torch.cuda.device(cuda_device):
+        want = _with_workspace(lib, q, k, p, cuda_device)
+        first = _no_alloc(lib, q, k, p, cuda_device)
+        second = _no_alloc(lib, q, k, p, cuda_device)
+    torch.cuda.synchronize()
+    n_summary = 10  # entries ADA_SUM_NE .. ADA_SUM_N_TOTAL; the rest are reserved
+    for got in (first, second):
+        assert torch.equal(got[0], want[0])
+        torch.testing.assert_close(got[1], want[1], rtol=0, atol=0, equal_nan=True)
+        torch.testing.assert_close(got[2][:n_summary], want[2][:n_summary], rtol=0, atol=0,
+                                   equal_nan=True)
+
+
+def test_no_alloc_refuses_more_heads_than_its_scratch(cuda_device):
+    lib = _lib.load()
+    base = torch.zeros(1, 1, 8, 64, device=cuda_device)
+    big = base.expand(1, LIMIT + 1, 8, 64)  # stride 0 over heads: no memory behind it
+    p = _params(0.125, 0)
+    dec = torch.empty(2, dtype=torch.int32, device=cuda_device)
+    st = torch.empty(4, dtype=torch.float32, device=cuda_device)
+    sm = torch.empty(_lib.SUMMARY_LEN, dtype=torch.float32, device=cuda_device)
+    with torch.cuda.device(cuda_device):
+        rc = lib.ada_analyze_noalloc(_lib.tensor(big), _lib.tensor(big), p, dec.data_ptr(),
+                                     st.data_ptr(), sm.data_ptr(), _lib.stream_ptr(cuda_device))
+    assert rc == -9  # ADA_ERR_UNSUPPORTED
+    assert "65536" in _lib.last_error()
