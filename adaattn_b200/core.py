@@ -34,6 +34,7 @@ class DecisionTable:
     head_stats: torch.Tensor
     summary: torch.Tensor
     granularity: str
+    head_sum: Optional[torch.Tensor] = None  # [B, H] sums of normalised row entropies
 
     @property
     def precision(self) -> torch.Tensor:
@@ -111,7 +112,8 @@ def analyze(q: torch.Tensor, k: torch.Tensor, *, scale: float, eps: float = 1e-6
                              summary.data_ptr(), ws.data_ptr(), ws.numel(),
                              _lib.stream_ptr(dev))
     _lib.check(rc, "ada_analyze")
-    return DecisionTable(decisions, stats, summary, granularity)
+    head_sum = ws[:b * h * 4].view(torch.float32).view(b, h) if b * h else None
+    return DecisionTable(decisions, stats, summary, granularity, head_sum)
 
 
 def expand_mask(mask: Optional[torch.Tensor], b: int, h: int, nq: int, nk: int

@@ -30,7 +30,7 @@ import torch.nn.functional as F
 
 __all__ = [
     "FP32", "FP16", "BF16", "FP8", "AUTO", "PREC_NAMES", "compute_dtype",
-    "OracleConfig", "sample_stats", "decide", "analyze", "analyze_per_head",
+    "OracleConfig", "sample_stats", "head_entropy_sums", "decide", "analyze", "analyze_per_head",
     "apply_masks", "dense_attention", "low_rank_attention", "adaptive_forward",
     "module_forward",
     "fp8_quantize_tiles", "fp8_dense_attention", "randomized_svd",
@@ -93,6 +93,28 @@ def sample_stats(q: torch.Tensor, k: torch.Tensor, scale: float, eps: float
     row_entropy = -(probs * torch.log(probs + eps)).sum(dim=-1)
     ne = (row_entropy / math.log(s)).mean().item()
     return ne, scores.abs().max().item(), probs.max().item(), s
+
+
+def head_entropy_sums(q: torch.Tensor, k: torch.Tensor, scale: float, eps: float
+                      ) -> Tuple[torch.Tensor, torch.Tensor, int]:
+    """Per-(b, h) pieces of the analyzer's call-level statistics.
+
+    Same arithmetic as sample_stats (adaattn.py:248-263) up to the mean: the
+    per-row normalised entropies (in the inputs' dtype), summed per slice in
+    fp32, and per-slice max |score| and max prob. Returns (sums [B, H],
+    stats [B, H, 4] with max|score| at [..., 1] and max prob at [..., 2], S).
+    """
+    n_q, n_k = q.shape[2], k.shape[2]
+    s = min(64, n_q, n_k)
+    scores = torch.matmul(q[:, :, :s], k[:, :, :s].transpose(-2, -1)) * scale
+    probs = F.softmax(scores, dim=-1)
+    row_entropy = -(probs * torch.log(probs + eps)).sum(dim=-1)
+    ne_rows = row_entropy / math.log(s)
+    sums = ne_rows.float().sum(dim=-1)
+    stats = torch.zeros(*q.shape[:2], 4)
+    stats[..., 1] = scores.abs().amax(dim=(-1, -2)).float()
+    stats[..., 2] = probs.amax(dim=(-1, -2)).float()
+    return sums, stats, s
 
 
 def decide(ne: float, max_score: float, max_prob: float, cfg: OracleConfig
