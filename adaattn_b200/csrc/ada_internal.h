@@ -123,6 +123,29 @@ struct PrepLaunch {
     int64_t nt_q, nt_k;
 };
 int launch_prep16(const PrepLaunch& L, cudaStream_t stream);
+
+// Tensor-core projection of q and k for low-rank heads (16-bit inputs,
+// D in {64, 128}); outputs as in PrepLaunch's 16-bit / fp32 regions.
+struct ProjLaunch {
+    CUtensorMap tq, tk;  // [B,H,N,D] inputs, 64-column x 128-row boxes
+    CUtensorMap tw;      // rank_proj_down.weight [r, D], 64-column x r_pad-row boxes
+    DecisionSrc dec;
+    int in_dtype;
+    int64_t B, H, Nq, Nk;
+    int D, r, r_pad;
+    uint32_t tc16_mask, f16_mask, fp32_mask;
+    void* ws16_q;
+    void* ws16_k;
+    int64_t ld16;
+    float* ws32_q;
+    float* ws32_k;
+    unsigned int* status;
+    uint64_t timeout_ns;
+};
+int launch_proj_tc(const ProjLaunch& L, cudaStream_t stream);
+// Vectorised casts for the 16-bit operand region: every tensor of dense heads
+// that are cast, only V for low-rank heads (their q, k come from the projection).
+int launch_cast16(const PrepLaunch& L, int skip_low_rank_qk, cudaStream_t stream);
 int launch_prep32(const PrepLaunch& L, cudaStream_t stream);
 int launch_prep8(const PrepLaunch& L, cudaStream_t stream);
 

@@ -158,6 +158,24 @@ int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int eb,
     return ADA_OK;
 }
 
+// 2-D map over a contiguous row-major [rows, width] 16-bit matrix with a
+// box_rows x 128-byte box and 128-byte swizzle (rows past the end read zero).
+int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int64_t width, int64_t rows,
+                int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int rc = encoder(&enc);
+    if (rc) return rc;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(width * 2)};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ADA_ERR_LAYOUT, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return ADA_OK;
+}
+
 CUtensorMapDataType tma_dtype(int dtype) {
     switch (dtype) {
         case ADA_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -253,8 +271,10 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
     P->direct_ok = (P->in_dtype == ADA_F16 || P->in_dtype == ADA_BF16) && (P->D == 64 || P->D == 128) &&
                    tma_ok(q) && tma_ok(k) && tma_ok(v);
     P->dqk_dense = pad_width(P->D);
-    P->dv_pad = pad_width(P->D);
     P->dqk_low = P->low_possible ? pad_width(P->r) : 0;
+    // A rank wider than a 64-wide head pads V to 128 as well: the kernels
+    // pair a 128-wide Q K^T only with a 128-wide P V.
+    P->dv_pad = P->dqk_low > pad_width(P->D) ? P->dqk_low : pad_width(P->D);
     P->ld16_qk = P->dqk_dense > P->dqk_low ? P->dqk_dense : P->dqk_low;
     P->ld16_v = P->dv_pad;
     P->need16 = false;
@@ -506,16 +526,56 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
     pl.fp8_mask = P.fp8_mask;
     pl.nt_q = P.nt_q;
     pl.nt_k = P.nt_k;
+    // Low-rank q/k projection on the tensor cores when the inputs are 16-bit
+    // and TMA-readable; the SIMT projection kernels cover every other case.
+    const int r_pad = P.low_possible ? pad_width(P.r) : 0;
+    const bool proj_tc = P.low_possible && (P.need16 || P.need32) && P.direct_ok &&
+                         (reinterpret_cast<uintptr_t>(w_down->data) & 15u) == 0 &&
+                         ((P.D == 128 && (r_pad == 64 || r_pad == 128)) || (P.D == 64 && r_pad == 64));
     if (P.need16) {
         pl.ws16_q = ws + P.off16q;
         pl.ws16_k = ws + P.off16k;
         pl.ws16_v = ws + P.off16v;
-        if ((rc = launch_prep16(pl, s))) return fail(rc, "prep16 launch failed");
+        if (proj_tc || !P.low_possible) {
+            if ((rc = launch_cast16(pl, proj_tc ? 1 : 0, s))) return fail(rc, "operand cast launch failed");
+        } else if ((rc = launch_prep16(pl, s))) {
+            return fail(rc, "prep16 launch failed");
+        }
     }
     if (P.need32) {
         pl.ws32_q = reinterpret_cast<float*>(ws + P.off32q);
         pl.ws32_k = reinterpret_cast<float*>(ws + P.off32k);
-        if ((rc = launch_prep32(pl, s))) return fail(rc, "prep32 launch failed");
+        if (!proj_tc && (rc = launch_prep32(pl, s))) return fail(rc, "prep32 launch failed");
+    }
+    if (proj_tc) {
+        ProjLaunch pj;
+        std::memset(&pj, 0, sizeof(pj));
+        const CUtensorMapDataType dt = tma_dtype(P.in_dtype);
+        if ((rc = make_map(&pj.tq, q->data, dt, 2, P.D, P.Nq, P.H, P.B, q->stride[2], q->stride[1], q->stride[0])) ||
+            (rc = make_map(&pj.tk, k->data, dt, 2, P.D, P.Nk, P.H, P.B, k->stride[2], k->stride[1], k->stride[0])) ||
+            (rc = make_map_2d(&pj.tw, w_down->data, dt, P.D, P.r, r_pad)))
+            return rc;
+        pj.dec = dsrc;
+        pj.in_dtype = P.in_dtype;
+        pj.B = P.B;
+        pj.H = P.H;
+        pj.Nq = P.Nq;
+        pj.Nk = P.Nk;
+        pj.D = static_cast<int>(P.D);
+        pj.r = static_cast<int>(P.r);
+        pj.r_pad = r_pad;
+        // Only precisions whose operand region exists are written.
+        pj.tc16_mask = P.need16 ? (P.tc16_mask & P.possible) : 0u;
+        pj.f16_mask = P.f16_mask;
+        pj.fp32_mask = P.need32 ? (P.fp32_mask & P.possible) : 0u;
+        pj.ws16_q = pl.ws16_q;
+        pj.ws16_k = pl.ws16_k;
+        pj.ld16 = P.ld16_qk;
+        pj.ws32_q = pl.ws32_q;
+        pj.ws32_k = pl.ws32_k;
+        pj.status = st;
+        pj.timeout_ns = wait_timeout_ns();
+        if ((rc = launch_proj_tc(pj, s))) return fail(rc, "tensor-core projection launch failed");
     }
     if (P.need8) {
         pl.ws8_q = ws + P.off8q;

@@ -126,6 +126,82 @@ __global__ void __launch_bounds__(kThreads) prep16_kernel(const __grid_constant_
     }
 }
 
+// Copy 64 rows of x [B,H,N,D] (row stride st[2]) into a 16-bit region row of
+// `width` columns in dtype cd, zero padded past D; 8 elements per thread step,
+// 16-byte accesses when `vec` says the source allows it.
+__device__ void cast_rows(const void* x, int in_dtype, const int64_t* st, int64_t b, int64_t h, int64_t row0,
+                          int64_t nrows, int D, uint16_t* dst_plane, int64_t ld, int width, int cd, bool vec) {
+    const int groups = width / 8;
+    const int64_t base = b * st[0] + h * st[1];
+    for (int i = threadIdx.x; i < kRows * groups; i += kThreads) {
+        const int rr = i / groups, g = i - rr * groups;
+        const int64_t grow = row0 + rr;
+        if (grow >= nrows) continue;
+        const int c0 = g * 8;
+        float v[8];
+        if (vec && c0 + 8 <= D) {
+            const int64_t e = base + grow * st[2] + c0;
+            if (in_dtype == ADA_F32) {
+                const float4 a = reinterpret_cast<const float4*>(x)[e / 4];
+                const float4 c = reinterpret_cast<const float4*>(x)[e / 4 + 1];
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+                v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+            } else {
+                const uint4 a = reinterpret_cast<const uint4*>(x)[e / 8];
+                const uint32_t w4[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (in_dtype == ADA_BF16) {
+                        const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(&w4[k]);
+                        v[2 * k] = __low2float(p);
+                        v[2 * k + 1] = __high2float(p);
+                    } else {
+                        const __half2 p = *reinterpret_cast<const __half2*>(&w4[k]);
+                        v[2 * k] = __low2float(p);
+                        v[2 * k + 1] = __high2float(p);
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                v[k] = (c0 + k < D) ? load_as_f32(x, base + grow * st[2] + (c0 + k) * st[3], in_dtype) : 0.f;
+        }
+        uint32_t p[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            p[k] = cd == ADA_F16 ? pack_f16x2(v[2 * k], v[2 * k + 1]) : pack_bf16x2(v[2 * k], v[2 * k + 1]);
+        reinterpret_cast<uint4*>(dst_plane + grow * ld)[g] = make_uint4(p[0], p[1], p[2], p[3]);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) cast16_kernel(const __grid_constant__ PrepLaunch L,
+                                                          int skip_low_rank_qk, int vec_q, int vec_k,
+                                                          int vec_v) {
+    const int64_t bh = blockIdx.y;
+    int prec, low;
+    get_decision(L.dec, bh, &prec, &low);
+    if (!((L.tc16_mask >> prec) & 1u)) return;
+    const int cd = ((L.f16_mask >> prec) & 1u) ? ADA_F16 : ADA_BF16;
+    if (!(low || cd != L.in_dtype || !L.direct_ok)) return;
+    const int64_t b = bh / L.H, h = bh % L.H;
+    const int D = static_cast<int>(L.D);
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
+    if (!(low && skip_low_rank_qk)) {
+        if (row0 < L.Nq)
+            cast_rows(L.q, L.in_dtype, L.qs, b, h, row0, L.Nq, D,
+                      reinterpret_cast<uint16_t*>(L.ws16_q) + bh * L.Nq * L.ld16_qk, L.ld16_qk, L.dqk_dense, cd,
+                      vec_q != 0);
+        if (row0 < L.Nk)
+            cast_rows(L.k, L.in_dtype, L.ks, b, h, row0, L.Nk, D,
+                      reinterpret_cast<uint16_t*>(L.ws16_k) + bh * L.Nk * L.ld16_qk, L.ld16_qk, L.dqk_dense, cd,
+                      vec_k != 0);
+    }
+    if (row0 < L.Nk)
+        cast_rows(L.v, L.in_dtype, L.vs, b, h, row0, L.Nk, D,
+                  reinterpret_cast<uint16_t*>(L.ws16_v) + bh * L.Nk * L.ld16_v, L.ld16_v, L.dv_pad, cd, vec_v != 0);
+}
+
 __global__ void __launch_bounds__(kThreads) prep32_kernel(const __grid_constant__ PrepLaunch L) {
     extern __shared__ float sm[];
     const int64_t bh = blockIdx.y;
@@ -288,6 +364,22 @@ int launch_prep16(const PrepLaunch& L, cudaStream_t stream) {
     const size_t smem = proj_smem(L, L.w_down != nullptr);
     if (set_smem(prep16_kernel, smem) != ADA_OK) return ADA_ERR_LAUNCH;
     prep16_kernel<<<dim3(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H)), kThreads, smem, stream>>>(L);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+int launch_cast16(const PrepLaunch& L, int skip_low_rank_qk, cudaStream_t stream) {
+    const int64_t nt = ((L.Nq > L.Nk ? L.Nq : L.Nk) + kRows - 1) / kRows;
+    if (nt == 0 || L.B * L.H == 0) return ADA_OK;
+    const int eb = L.in_dtype == ADA_F32 ? 4 : 2;
+    auto vec_ok = [&](const void* p, const int64_t* st) {
+        if (st[3] != 1 || (L.D % 8) != 0) return 0;
+        if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return 0;
+        for (int i = 0; i < 3; ++i)
+            if (((st[i] * eb) % 16) != 0) return 0;
+        return 1;
+    };
+    cast16_kernel<<<dim3(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H)), kThreads, 0, stream>>>(
+        L, skip_low_rank_qk, vec_ok(L.q, L.qs), vec_ok(L.k, L.ks), vec_ok(L.v, L.vs));
     return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
 

@@ -89,6 +89,12 @@ LOW_CASES = [
     (torch.bfloat16, O.FP32, 128, 64, 200),
     (torch.float32, O.FP16, 64, 32, 256),
     (torch.float32, O.FP32, 64, 32, 129),
+    # 16-bit inputs with D in {64, 128}: projection on the tensor cores
+    (torch.float16, O.FP16, 64, 32, 200),
+    (torch.bfloat16, O.BF16, 128, 128, 256),
+    (torch.bfloat16, O.FP16, 128, 100, 190),
+    (torch.float16, O.FP32, 128, 64, 140),
+    (torch.bfloat16, O.BF16, 64, 100, 128),    # r_pad 128 > D: SIMT projection
 ]
 
 
