@@ -9,7 +9,8 @@ throughput. FLOPs follow the dense convention 4 B H Nq Nk D (halved under
 causal masking); low-rank heads add their projection and use r for Q K^T.
 The gpt2_small workload times a 12-layer, 768-wide decoder forward built from
 AdaAttention (the reference's examples/transformer_integration.py shape) and
-reports tokens/s.
+reports tokens/s. The rsvd workload times the randomized SVD of the low-rank
+workload's K heads (64 fp32 matrices of 8192 x 128, rank 64).
 """
 
 from __future__ import annotations
@@ -112,16 +113,42 @@ def gpt2_workload(steps: int) -> dict:
             "low_rank_ratio_layer0": stats[0]["low_rank_ratio"]}
 
 
+def rsvd_workload(steps: int, n_power: int) -> dict:
+    """Randomized SVD of the K heads of the low-rank workload: 64 fp32
+    matrices of 8192 x 128, rank 64 (k = 74), one sketch per head."""
+    from .linalg import randomized_svd, sketch_width
+    w = WORKLOADS["low_rank_mix"]
+    _, k, _ = make_qkv(w, seed=0, device="cuda")
+    a = k.float().reshape(-1, w.seq, w.head_dim).contiguous()
+    rank = w.head_dim // 2
+    kw = sketch_width(rank, w.seq, w.head_dim)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    omega = torch.randn(a.shape[0], w.head_dim, kw, device="cuda", generator=g)
+
+    def step():
+        return randomized_svd(a, rank, num_power_iterations=n_power, omega=omega)
+
+    ms = _time(step, steps)
+    passes = 2 + 2 * n_power  # A is read by A Omega, each power step (twice) and Q^T A
+    return {"workload": "rsvd_k_heads", "shape": f"{a.shape[0]} x {w.seq} x {w.head_dim} fp32",
+            "rank": rank, "sketch": kw, "n_power": n_power, "ms": ms,
+            "a_passes": passes, "a_gbs": passes * a.numel() * 4 / (ms * 1e-3) / 1e9,
+            "matrices_per_s": a.shape[0] / (ms * 1e-3)}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", default="all",
-                    choices=["all", "adaptive_mix", "low_rank_mix", "precision_mix", "gpt2_small"])
+                    choices=["all", "adaptive_mix", "low_rank_mix", "precision_mix", "gpt2_small", "rsvd"])
     ap.add_argument("--steps", type=int, default=10)
     args = ap.parse_args(argv)
-    todo = ["adaptive_mix", "low_rank_mix", "precision_mix", "gpt2_small"] \
+    todo = ["adaptive_mix", "low_rank_mix", "precision_mix", "gpt2_small", "rsvd"] \
         if args.workload == "all" else [args.workload]
     for name in todo:
-        if name == "gpt2_small":
+        if name == "rsvd":
+            for n_power in (1, 2):
+                print(json.dumps(rsvd_workload(args.steps, n_power)), flush=True)
+        elif name == "gpt2_small":
             print(json.dumps(gpt2_workload(args.steps)), flush=True)
         elif name == "precision_mix":
             for allow in (False, True):

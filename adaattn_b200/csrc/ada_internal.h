@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -36,6 +37,12 @@ int launch_target_ranks(const float* eff, int64_t n, int64_t min_rank, int64_t m
 int launch_bounded_wait(uint64_t timeout_ns, unsigned int* status, cudaStream_t stream);
 // Sets the calling thread's ada_get_last_error message; returns `code`.
 int record_last_error(int code, const char* msg);
+// Checks for an sm_100 device and resolves its status word (once per device).
+int device_status_word(unsigned int** status);
+// cuTensorMapEncodeTiled from the driver (resolved once).
+int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn);
+// Limit of every bounded device-side wait (ADA_WAIT_TIMEOUT_MS, default 4 s).
+uint64_t default_wait_timeout_ns();
 
 // --- which heads a launch serves ---------------------------------------------
 // A head (b,h) is served when decisions == nullptr (static decision) or when

@@ -368,6 +368,9 @@ void copy_strides(int64_t* dst, const AdaTensor* t) {
 namespace ada {
 // Lets entry points defined in other files report through ada_get_last_error.
 int record_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+int device_status_word(unsigned int** status) { return device_setup(status); }
+int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) { return encoder(fn); }
+uint64_t default_wait_timeout_ns() { return wait_timeout_ns(); }
 }  // namespace ada
 
 using namespace ada;

@@ -189,6 +189,22 @@ int         ada_determine_target_ranks(const float* effective_rank, int64_t n,
                                        int64_t min_rank, int64_t max_rank, double threshold,
                                        int64_t* ranks_out, void* stream);
 
+/* Randomized truncated SVD of a batch of fp32 matrices, A ~= U diag(S) Vh;
+ * replaces adaattn.linalg.low_rank.randomized_svd
+ * (src/adaattn/linalg/low_rank.py:56-109) with the Gaussian sketch passed in.
+ *   a      [batch, m, n] fp32 (any strides; copied when TMA cannot read it)
+ *   omega  [batch, n, k] fp32, k = min(rank + oversampling, min(m, n)) <= 112
+ *   n_power power iterations Y = A (A^T Y) (the reference uses 2)
+ *   u [batch, m, rank], s [batch, rank] (descending), vh [batch, rank, n] fp32
+ * The basis of range(Y) comes from CholeskyQR2 instead of Householder QR; a
+ * sketch column that is numerically inside the span of the earlier ones
+ * gives a zero basis column. Workspace: 256-byte aligned,
+ * ada_rsvd_workspace_bytes() bytes (0 when the arguments are invalid). */
+size_t      ada_rsvd_workspace_bytes(const AdaTensor* a, const AdaTensor* omega, int32_t rank);
+int         ada_rsvd(const AdaTensor* a, const AdaTensor* omega, int32_t rank, int32_t n_power,
+                     AdaTensor* u, AdaTensor* s, AdaTensor* vh,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
 /* Test hook for failure detection: launches one block that waits on a device
  * barrier nothing ever signals, bounded by `timeout_ns`; the wait gives up,
  * records ADA_ERR_TIMEOUT in the status word and the kernel returns normally. */
