@@ -61,9 +61,27 @@ struct PanelGemm {
     int kdim;  // reduction extent: n (NN) or m (TN)
     int k, kp;
     int trans;  // 0: out = (A X)^T; 1: out = (A^T Y)^T
+    int batch, tiles;     // work items: (batch, 128-row tile, K split)
+    int splits, cps;      // K splits per tile, 32-wide chunks per split
     unsigned int* status;
     uint64_t timeout_ns;
 };
+
+// Work item it -> (b, tile, split) and its chunk range [c0, c1).
+struct PgItem {
+    int b, row0, c0, c1;
+};
+__device__ __forceinline__ PgItem pg_item(const PanelGemm& G, int it) {
+    PgItem w;
+    const int split = it % G.splits;
+    const int bt = it / G.splits;
+    w.b = bt / G.tiles;
+    w.row0 = (bt % G.tiles) * 128;
+    const int nchunks = (G.kdim + 31) / 32;
+    w.c0 = split * G.cps;
+    w.c1 = min(nchunks, w.c0 + G.cps);
+    return w;
+}
 
 __device__ __forceinline__ void split_tf32(float4& v, float4& lo) {
     float h[4] = {v.x, v.y, v.z, v.w}, l[4];
@@ -117,15 +135,17 @@ __device__ __forceinline__ void pg_split_stage(uint8_t* stage, int t) {
     fence_proxy_async_smem();
 }
 
+// Persistent CTAs walk the work items with a static stride; the TMA / MMA /
+// split pipeline runs across item boundaries. With several K splits per
+// tile the item's partial result is added to the zeroed output with fp32
+// atomics (round-to-nearest, order-dependent in the last bit).
 template <int KP>
 __global__ void __launch_bounds__(kPgThreads, 1) panel_gemm_kernel(const __grid_constant__ PanelGemm G) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     PgBarriers* bars = reinterpret_cast<PgBarriers*>(base + kPgStages * kPgStageBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b = blockIdx.y;
-    const int row0 = blockIdx.x * 128;
-    const int nchunks = (G.kdim + 31) / 32;
+    const int n_items = G.batch * G.tiles * G.splits;
     constexpr uint32_t P_BYTES = KP * 128u;
 
     if (threadIdx.x == 0) {
@@ -156,62 +176,71 @@ __global__ void __launch_bounds__(kPgThreads, 1) panel_gemm_kernel(const __grid_
         if (lane == 0) {
             tma_prefetch_desc(&G.ta);
             tma_prefetch_desc(&G.tp);
-            for (int c = 0; c < nchunks; ++c) {
-                const int st = c % kPgStages;
-                const uint32_t ph = (c / kPgStages) & 1u;
-                if (!mbar_wait(smem_u32(&bars->empty[st]), ph ^ 1u, abort_flag, tmo, G.status)) break;
-                const uint32_t fb = smem_u32(&bars->full[st]);
-                mbar_arrive_expect_tx(fb, kPgHalf + P_BYTES);
-                uint8_t* sa = base + st * kPgStageBytes;
-                if (!G.trans) {
-                    tma_load_3d(smem_u32(sa), &G.ta, fb, c * 32, row0, b);
-                } else {
+            int g = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+                const PgItem w = pg_item(G, it);
+                for (int c = w.c0; c < w.c1; ++c, ++g) {
+                    const int st = g % kPgStages;
+                    const uint32_t ph = (g / kPgStages) & 1u;
+                    ok = mbar_wait(smem_u32(&bars->empty[st]), ph ^ 1u, abort_flag, tmo, G.status);
+                    if (!ok) break;
+                    const uint32_t fb = smem_u32(&bars->full[st]);
+                    mbar_arrive_expect_tx(fb, kPgHalf + P_BYTES);
+                    uint8_t* sa = base + st * kPgStageBytes;
+                    if (!G.trans) {
+                        tma_load_3d(smem_u32(sa), &G.ta, fb, c * 32, w.row0, w.b);
+                    } else {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        tma_load_3d(smem_u32(sa + q * 4096), &G.ta, fb, row0 + 32 * q, c * 32, b);
+                        for (int q = 0; q < 4; ++q)
+                            tma_load_3d(smem_u32(sa + q * 4096), &G.ta, fb, w.row0 + 32 * q, c * 32, w.b);
+                    }
+                    tma_load_3d(smem_u32(sa + 2 * kPgHalf), &G.tp, fb, c * 32, 0, w.b);
                 }
-                tma_load_3d(smem_u32(sa + 2 * kPgHalf), &G.tp, fb, c * 32, 0, b);
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = make_idesc(2, 2, G.trans ? 1u : 0u, 0, 128, KP);
-            int issued = 0;
-            for (int c = 0; c < nchunks; ++c) {
-                const int st = c % kPgStages;
-                const uint32_t ph = (c / kPgStages) & 1u;
-                const int ab = c & 1;
-                if (!mbar_wait(smem_u32(&bars->acc_empty[ab]), ((c >> 1) & 1u) ^ 1u, abort_flag, tmo, G.status))
-                    break;
-                if (!mbar_wait(smem_u32(&bars->split[st]), ph, abort_flag, tmo, G.status)) break;
-                tc_fence_after();
-                const uint32_t ah = smem_u32(base + st * kPgStageBytes);
-                const uint32_t al = ah + kPgHalf, phd = ah + 2 * kPgHalf, pl = ah + 3 * kPgHalf;
-                const uint32_t d_head = tmem + ab * 256, d_tail = d_head + 128;
+            int g = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+                const PgItem w = pg_item(G, it);
+                for (int c = w.c0; c < w.c1; ++c, ++g) {
+                    const int st = g % kPgStages;
+                    const uint32_t ph = (g / kPgStages) & 1u;
+                    const int ab = g & 1;
+                    ok = mbar_wait(smem_u32(&bars->acc_empty[ab]), ((g >> 1) & 1u) ^ 1u, abort_flag, tmo, G.status);
+                    if (ok) ok = mbar_wait(smem_u32(&bars->split[st]), ph, abort_flag, tmo, G.status);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t ah = smem_u32(base + st * kPgStageBytes);
+                    const uint32_t al = ah + kPgHalf, phd = ah + 2 * kPgHalf, pl = ah + 3 * kPgHalf;
+                    const uint32_t d_head = tmem + ab * 256, d_tail = d_head + 128;
 #pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    uint64_t dah, dal;
-                    if (!G.trans) {
-                        dah = make_sdesc_sw128(ah + s * 32, 16, 1024);
-                        dal = make_sdesc_sw128(al + s * 32, 16, 1024);
-                    } else {
-                        dah = make_sdesc_mn32(ah + s * 1024);
-                        dal = make_sdesc_mn32(al + s * 1024);
+                    for (int s = 0; s < 4; ++s) {
+                        uint64_t dah, dal;
+                        if (!G.trans) {
+                            dah = make_sdesc_sw128(ah + s * 32, 16, 1024);
+                            dal = make_sdesc_sw128(al + s * 32, 16, 1024);
+                        } else {
+                            dah = make_sdesc_mn32(ah + s * 1024);
+                            dal = make_sdesc_mn32(al + s * 1024);
+                        }
+                        const uint64_t dph = make_sdesc_sw128(phd + s * 32, 16, 1024);
+                        const uint64_t dpl = make_sdesc_sw128(pl + s * 32, 16, 1024);
+                        mma_ss_tf32(d_tail, dal, dph, idesc, s > 0 ? 1u : 0u);
+                        mma_ss_tf32(d_tail, dah, dpl, idesc, 1u);
+                        mma_ss_tf32(d_head, dah, dph, idesc, s > 0 ? 1u : 0u);
                     }
-                    const uint64_t dph = make_sdesc_sw128(phd + s * 32, 16, 1024);
-                    const uint64_t dpl = make_sdesc_sw128(pl + s * 32, 16, 1024);
-                    mma_ss_tf32(d_tail, dal, dph, idesc, s > 0 ? 1u : 0u);
-                    mma_ss_tf32(d_tail, dah, dpl, idesc, 1u);
-                    mma_ss_tf32(d_head, dah, dph, idesc, s > 0 ? 1u : 0u);
+                    tc_commit(smem_u32(&bars->empty[st]));
+                    tc_commit(smem_u32(&bars->acc_full[ab]));
                 }
-                tc_commit(smem_u32(&bars->empty[st]));
-                tc_commit(smem_u32(&bars->acc_full[ab]));
-                issued = c + 1;
             }
-            if (issued > 0) {
+            if (g > 0) {
                 // bounded wait for the last products before the CTA frees TMEM
-                const int c = issued - 1;
+                const int c = g - 1;
                 const uint64_t t0 = globaltimer_ns();
                 uint32_t spins = 0;
                 while (!mbar_try_wait(smem_u32(&bars->acc_full[c & 1]), (c >> 1) & 1u)) {
@@ -226,45 +255,71 @@ __global__ void __launch_bounds__(kPgThreads, 1) panel_gemm_kernel(const __grid_
     } else if (warp >= 4) {
         const int t = threadIdx.x - 128;
         const uint32_t lane_bits = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const int rrow = (warp & 3) * 32 + lane;
         float acc[KP];
 #pragma unroll
         for (int i = 0; i < KP; ++i) acc[i] = 0.f;
-        bool ok = true;
-        auto add_chunk = [&](int c) -> bool {
-            const int ab = c & 1;
-            if (!mbar_wait(smem_u32(&bars->acc_full[ab]), (c >> 1) & 1u, abort_flag, tmo, G.status)) return false;
+        auto add_chunk = [&](int g) -> bool {
+            const int ab = g & 1;
+            if (!mbar_wait(smem_u32(&bars->acc_full[ab]), (g >> 1) & 1u, abort_flag, tmo, G.status)) return false;
             tc_fence_after();
 #pragma unroll
-            for (int cc = 0; cc < KP / 32; ++cc) {
-                uint32_t h[32], l[32];
-                tmem_ld32(tmem + lane_bits + ab * 256 + cc * 32, h);
-                tmem_ld32(tmem + lane_bits + ab * 256 + 128 + cc * 32, l);
+            for (int cc = 0; cc < KP / 16; ++cc) {
+                uint32_t h[16], l[16];
+                tmem_ld16(tmem + lane_bits + ab * 256 + cc * 16, h);
+                tmem_ld16(tmem + lane_bits + ab * 256 + 128 + cc * 16, l);
                 tmem_ld_wait();
-                reg_fence32(h);
-                reg_fence32(l);
+                reg_fence16(h);
+                reg_fence16(l);
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    acc[cc * 32 + i] += __uint_as_float(h[i]) + __uint_as_float(l[i]);
+                for (int i = 0; i < 16; ++i)
+                    acc[cc * 16 + i] += __uint_as_float(h[i]) + __uint_as_float(l[i]);
             }
             tc_fence_before();
             mbar_arrive(smem_u32(&bars->acc_empty[ab]));
             return true;
         };
-        for (int c = 0; ok && c < nchunks; ++c) {
-            const int st = c % kPgStages;
-            ok = mbar_wait(smem_u32(&bars->full[st]), (c / kPgStages) & 1u, abort_flag, tmo, G.status);
-            if (!ok) break;
-            pg_split_stage<KP>(base + st * kPgStageBytes, t);
-            mbar_arrive(smem_u32(&bars->split[st]));
-            if (c > 0) ok = add_chunk(c - 1);
-        }
-        if (ok) ok = add_chunk(nchunks - 1);
-        const int grow = row0 + (warp & 3) * 32 + lane;
-        if (ok && grow < G.rows) {
-            float* o = G.out + b * G.out_bs + grow;
+        auto store = [&](const PgItem& w) {
+            const int grow = w.row0 + rrow;
+            if (grow < G.rows) {
+                float* o = G.out + w.b * G.out_bs + grow;
+                if (G.splits == 1) {
 #pragma unroll
-            for (int i = 0; i < KP; ++i)
-                if (i < G.k) o[i * G.ld_out] = acc[i];
+                    for (int i = 0; i < KP; ++i)
+                        if (i < G.k) o[i * G.ld_out] = acc[i];
+                } else {
+#pragma unroll
+                    for (int i = 0; i < KP; ++i)
+                        if (i < G.k) atomicAdd(o + i * G.ld_out, acc[i]);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < KP; ++i) acc[i] = 0.f;
+        };
+        int g = 0;
+        bool ok = true, have_prev = false, prev_last = false;
+        PgItem prev_item{};
+        for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+            const PgItem w = pg_item(G, it);
+            for (int c = w.c0; c < w.c1; ++c, ++g) {
+                const int st = g % kPgStages;
+                ok = mbar_wait(smem_u32(&bars->full[st]), (g / kPgStages) & 1u, abort_flag, tmo, G.status);
+                if (!ok) break;
+                pg_split_stage<KP>(base + st * kPgStageBytes, t);
+                mbar_arrive(smem_u32(&bars->split[st]));
+                if (have_prev) {
+                    ok = add_chunk(g - 1);
+                    if (!ok) break;
+                    if (prev_last) store(prev_item);
+                }
+                have_prev = true;
+                prev_last = c == w.c1 - 1;
+                prev_item = w;
+            }
+        }
+        if (ok && have_prev) {
+            ok = add_chunk(g - 1);
+            if (ok && prev_last) store(prev_item);
         }
     }
     tc_fence_before();
@@ -279,60 +334,79 @@ __global__ void __launch_bounds__(kPgThreads, 1) panel_gemm_kernel(const __grid_
 // fp64 Gram of a panel: G[b] (upper triangle, zeroed by the caller) +=
 // P[b][:, i0:i0+256] P[b][:, i0:i0+256]^T, 4x4 blocks per thread.
 // ---------------------------------------------------------------------------
-constexpr int kGramCols = 256;
+constexpr int kGramCols = 128;   // columns staged per pass (as fp64)
+constexpr int kGramPasses = 4;   // passes per CTA before its atomics
 
 __global__ void __launch_bounds__(256) gram64_kernel(const float* P, int64_t p_bs, int64_t p_ld, int k, int L,
                                                      double* G) {
-    extern __shared__ float sp[];  // [k][kGramCols + 1]
+    extern __shared__ double sgd[];  // [k][kGramCols + 1]
     constexpr int LD = kGramCols + 1;
     const int b = blockIdx.y;
-    const int i0 = blockIdx.x * kGramCols;
-    const int w = min(kGramCols, L - i0);
     const float* src = P + b * p_bs;
-    for (int idx = threadIdx.x; idx < k * kGramCols; idx += blockDim.x) {
-        const int c = idx / kGramCols, i = idx - c * kGramCols;
-        sp[c * LD + i] = i < w ? src[c * p_ld + i0 + i] : 0.f;
-    }
-    __syncthreads();
     const int kb = (k + 3) / 4;
     const int npairs = kb * (kb + 1) / 2;
-    double* g = G + static_cast<int64_t>(b) * k * k;
-    for (int pi = threadIdx.x; pi < npairs; pi += blockDim.x) {
-        int bi = 0, rem = pi;
+    // 4x4 blocks of the upper triangle: k <= 112 gives at most 406, two slots per thread
+    constexpr int kSlots = 2;
+    int bi_s[kSlots], bj_s[kSlots];
+    double acc[kSlots][4][4];
+#pragma unroll
+    for (int sl = 0; sl < kSlots; ++sl) {
+        const int pi = threadIdx.x + sl * blockDim.x;
+        int bi = 0, rem = pi < npairs ? pi : 0;
         while (rem >= kb - bi) {
             rem -= kb - bi;
             ++bi;
         }
-        const int bj = bi + rem;
-        int ri[4], rj[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            ri[u] = min(4 * bi + u, k - 1) * LD;
-            rj[u] = min(4 * bj + u, k - 1) * LD;
-        }
-        double acc[4][4];
+        bi_s[sl] = pi < npairs ? bi : -1;
+        bj_s[sl] = bi + rem;
 #pragma unroll
         for (int u = 0; u < 4; ++u)
 #pragma unroll
-            for (int v = 0; v < 4; ++v) acc[u][v] = 0.0;
-        for (int i = 0; i < w; ++i) {
-            double x[4], y[4];
+            for (int v = 0; v < 4; ++v) acc[sl][u][v] = 0.0;
+    }
+    for (int pass = 0; pass < kGramPasses; ++pass) {
+        const int i0 = (blockIdx.x * kGramPasses + pass) * kGramCols;
+        if (i0 >= L) break;
+        const int w = min(kGramCols, L - i0);
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < k * kGramCols; idx += blockDim.x) {
+            const int c = idx / kGramCols, i = idx - c * kGramCols;
+            sgd[c * LD + i] = i < w ? static_cast<double>(src[c * p_ld + i0 + i]) : 0.0;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) {
+            if (bi_s[sl] < 0) continue;
+            int ri[4], rj[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                x[u] = static_cast<double>(sp[ri[u] + i]);
-                y[u] = static_cast<double>(sp[rj[u] + i]);
+                ri[u] = min(4 * bi_s[sl] + u, k - 1) * LD;
+                rj[u] = min(4 * bj_s[sl] + u, k - 1) * LD;
             }
+            for (int i = 0; i < w; ++i) {
+                double x[4], y[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+                for (int u = 0; u < 4; ++u) {
+                    x[u] = sgd[ri[u] + i];
+                    y[u] = sgd[rj[u] + i];
+                }
 #pragma unroll
-                for (int v = 0; v < 4; ++v) acc[u][v] = fma(x[u], y[v], acc[u][v]);
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) acc[sl][u][v] = fma(x[u], y[v], acc[sl][u][v]);
+            }
         }
+    }
+    double* g = G + static_cast<int64_t>(b) * k * k;
+#pragma unroll
+    for (int sl = 0; sl < kSlots; ++sl) {
+        if (bi_s[sl] < 0) continue;
 #pragma unroll
         for (int u = 0; u < 4; ++u)
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
-                const int r = 4 * bi + u, c = 4 * bj + v;
-                if (r < k && c < k && r <= c) atomicAdd(g + r * k + c, acc[u][v]);
+                const int r = 4 * bi_s[sl] + u, c = 4 * bj_s[sl] + v;
+                if (r < k && c < k && r <= c) atomicAdd(g + r * k + c, acc[sl][u][v]);
             }
     }
 }
@@ -397,7 +471,7 @@ __global__ void __launch_bounds__(256) chol_inv_kernel(const double* Gall, int k
 // eigenvalues sorted descending: S = sqrt(lambda), MU = eigenvectors[:, :r],
 // MV = MU / S (zero where S is zero). One CTA per matrix.
 // ---------------------------------------------------------------------------
-constexpr int kEigThreads = 256;
+constexpr int kEigThreads = 1024;
 
 __device__ double block_sum(double v, double* red) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -409,24 +483,72 @@ __device__ double block_sum(double v, double* red) {
     return s;
 }
 
+// Round-robin pairing: in round `round`, slot x meets slot kk-1-x; slot kk-1
+// stays put and the others rotate.
+__device__ __forceinline__ void rr_pair(int kk, int round, int pi, int* p, int* q) {
+    const int x0 = pi, x1 = kk - 1 - pi;
+    int a = x0 == kk - 1 ? kk - 1 : (x0 + round) % (kk - 1);
+    int b = x1 == kk - 1 ? kk - 1 : (x1 + round) % (kk - 1);
+    *p = a < b ? a : b;
+    *q = a < b ? b : a;
+}
+
+// 1/sqrt(x) and 1/x for x within the float range: an fp32 estimate refined
+// by two Newton steps in fp64 (y <- y (3 - x y^2) / 2, y <- y (2 - x y)),
+// each of which squares the relative error.
+__device__ __forceinline__ double rsqrt_newton(double x) {
+    double y = static_cast<double>(rsqrtf(static_cast<float>(x)));
+    y = y * fma(-0.5 * x * y, y, 1.5);
+    y = y * fma(-0.5 * x * y, y, 1.5);
+    return y;
+}
+__device__ __forceinline__ double rcp_newton(double x) {
+    double y = static_cast<double>(__frcp_rn(static_cast<float>(x)));
+    y = y * fma(-x, y, 2.0);
+    y = y * fma(-x, y, 2.0);
+    return y;
+}
+
+// Jacobi rotation (c, s) that zeroes a_pq: t = sign(d) e / (|d| + sqrt(d^2 +
+// e^2)) with d = a_qq - a_pp, e = 2 a_pq (the smaller root of
+// t^2 + 2 (d/e) t - 1 = 0), c = 1/sqrt(1 + t^2), s = t c. d and e are first
+// scaled by a power of two so every intermediate sits well inside the
+// float range of the Newton seeds.
+__device__ __forceinline__ void jacobi_rotation(double app, double aqq, double apq, double* c, double* s) {
+    const double d = aqq - app, e = 2.0 * apq;
+    const int ex = ilogb(fmax(fabs(d), fabs(e)));
+    const double ds = scalbn(d, -ex), es = scalbn(e, -ex);  // max(|ds|, |es|) in [1, 2)
+    const double h = fma(ds, ds, es * es);                  // in [1, 8)
+    const double r = h * rsqrt_newton(h);
+    const double t = (d >= 0.0 ? es : -es) * rcp_newton(fabs(ds) + r);
+    *c = rsqrt_newton(fma(t, t, 1.0));
+    *s = t * *c;
+}
+
+// Round structure: the rotations of all disjoint pairs are formed in
+// parallel (one thread each), then one warp per pair applies its rotation to
+// the two rows, and after a block barrier to the two columns of W and V.
 __global__ void __launch_bounds__(kEigThreads) eig_kernel(const double* Wall, int k, int r, float* s_out,
                                                           int64_t s_bs, int64_t s_st, double* mu_all,
                                                           double* mv_all, int max_sweeps) {
     extern __shared__ double smd[];
     const int kk = k + (k & 1);
-    double* a = smd;            // [kk][kk]
-    double* v = smd + kk * kk;  // [kk][kk]
+    const int ld = kk + 1;
+    double* a = smd;            // [kk][ld]
+    double* v = smd + kk * ld;  // [kk][ld]
     __shared__ double cs_c[kMaxSketch / 2], cs_s[kMaxSketch / 2];
-    __shared__ int pp[kMaxSketch / 2], qq[kMaxSketch / 2];
     __shared__ double red[kEigThreads / 32];
+    __shared__ int rotations;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
     const int b = blockIdx.x;
     const double* W = Wall + static_cast<int64_t>(b) * k * k;
     for (int idx = threadIdx.x; idx < kk * kk; idx += blockDim.x) {
         const int i = idx / kk, j = idx - i * kk;
         double val = 0.0;
         if (i < k && j < k) val = i <= j ? W[i * k + j] : W[j * k + i];
-        a[idx] = val;
-        v[idx] = i == j ? 1.0 : 0.0;
+        a[i * ld + j] = val;
+        v[i * ld + j] = i == j ? 1.0 : 0.0;
     }
     __syncthreads();
     const int half = kk / 2;
@@ -434,79 +556,88 @@ __global__ void __launch_bounds__(kEigThreads) eig_kernel(const double* Wall, in
         double off = 0.0, dg = 0.0;
         for (int idx = threadIdx.x; idx < kk * kk; idx += blockDim.x) {
             const int i = idx / kk, j = idx - i * kk;
-            const double e = a[idx] * a[idx];
+            const double e = a[i * ld + j] * a[i * ld + j];
             if (i == j) dg += e; else off += e;
         }
         off = block_sum(off, red);
         dg = block_sum(dg, red);
-        if (!(off > 1e-30 * dg)) break;
+        if (!(off > 1e-28 * dg)) break;
+        // Rotations are skipped once |a_pq| is within 100x of the rounding
+        // level next to its diagonal pair or next to the matrix norm (below
+        // that a rotation only moves rounding noise around); a sweep without
+        // any rotation ends the iteration.
+        const double tiny = 1e-14 * sqrt(dg);
+        if (threadIdx.x == 0) rotations = 0;
+        __syncthreads();
         for (int round = 0; round < kk - 1; ++round) {
-            if (threadIdx.x < half) {
-                const int x0 = threadIdx.x, x1 = kk - 1 - threadIdx.x;
-                int p = x0 == kk - 1 ? kk - 1 : (x0 + round) % (kk - 1);
-                int q = x1 == kk - 1 ? kk - 1 : (x1 + round) % (kk - 1);
-                if (p > q) {
-                    const int t = p;
-                    p = q;
-                    q = t;
-                }
-                const double apq = a[p * kk + q];
+            for (int pi = threadIdx.x; pi < half; pi += blockDim.x) {
+                int p, q;
+                rr_pair(kk, round, pi, &p, &q);
                 double c = 1.0, s = 0.0;
-                if (apq != 0.0) {
-                    const double tau = (a[q * kk + q] - a[p * kk + p]) / (2.0 * apq);
-                    const double t = (tau >= 0.0 ? 1.0 : -1.0) / (fabs(tau) + sqrt(1.0 + tau * tau));
-                    c = 1.0 / sqrt(1.0 + t * t);
-                    s = t * c;
+                const double apq = a[p * ld + q], app = a[p * ld + p], aqq = a[q * ld + q];
+                // |a_pq| > 1e-14 sqrt(|a_pp a_qq|), compared squared
+                if (fabs(apq) > tiny && apq * apq > 1e-28 * fabs(app * aqq)) {
+                    jacobi_rotation(app, aqq, apq, &c, &s);
+                    if (s != 0.0) atomicAdd(&rotations, 1);
                 }
-                pp[threadIdx.x] = p;
-                qq[threadIdx.x] = q;
-                cs_c[threadIdx.x] = c;
-                cs_s[threadIdx.x] = s;
+                cs_c[pi] = c;
+                cs_s[pi] = s;
             }
             __syncthreads();
-            for (int idx = threadIdx.x; idx < half * kk; idx += blockDim.x) {
-                const int pi = idx / kk, xx = idx - pi * kk;
+            for (int pi = warp; pi < half; pi += nwarps) {
+                const double s = cs_s[pi];
+                if (s != 0.0) {
+                    const double c = cs_c[pi];
+                    int p, q;
+                    rr_pair(kk, round, pi, &p, &q);
+                    for (int x = lane; x < kk; x += 32) {
+                        const double ap = a[p * ld + x], aq = a[q * ld + x];
+                        a[p * ld + x] = c * ap - s * aq;
+                        a[q * ld + x] = s * ap + c * aq;
+                    }
+                }
+            }
+            __syncthreads();
+            for (int pi = warp; pi < half; pi += nwarps) {
                 const double s = cs_s[pi];
                 if (s == 0.0) continue;
                 const double c = cs_c[pi];
-                const int p = pp[pi], q = qq[pi];
-                const double ap = a[p * kk + xx], aq = a[q * kk + xx];
-                a[p * kk + xx] = c * ap - s * aq;
-                a[q * kk + xx] = s * ap + c * aq;
-            }
-            __syncthreads();
-            for (int idx = threadIdx.x; idx < half * kk; idx += blockDim.x) {
-                const int pi = idx / kk, xx = idx - pi * kk;
-                const double s = cs_s[pi];
-                if (s == 0.0) continue;
-                const double c = cs_c[pi];
-                const int p = pp[pi], q = qq[pi];
-                const double ap = a[xx * kk + p], aq = a[xx * kk + q];
-                a[xx * kk + p] = c * ap - s * aq;
-                a[xx * kk + q] = s * ap + c * aq;
-                const double vp = v[xx * kk + p], vq = v[xx * kk + q];
-                v[xx * kk + p] = c * vp - s * vq;
-                v[xx * kk + q] = s * vp + c * vq;
+                int p, q;
+                rr_pair(kk, round, pi, &p, &q);
+                for (int x = lane; x < kk; x += 32) {
+                    const double ap = a[x * ld + p], aq = a[x * ld + q];
+                    a[x * ld + p] = c * ap - s * aq;
+                    a[x * ld + q] = s * ap + c * aq;
+                    const double vp = v[x * ld + p], vq = v[x * ld + q];
+                    v[x * ld + p] = c * vp - s * vq;
+                    v[x * ld + q] = s * vp + c * vq;
+                }
             }
             __syncthreads();
         }
+        if (rotations == 0) break;
+        __syncthreads();
     }
     for (int i = threadIdx.x; i < k; i += blockDim.x) {
-        const double d = a[i * kk + i];
+        const double d = a[i * ld + i];
         int rank = 0;
+        double dmax = 0.0;
         for (int j = 0; j < k; ++j) {
-            const double e = a[j * kk + j];
+            const double e = a[j * ld + j];
             if (e > d || (e == d && j < i)) ++rank;
+            dmax = fmax(dmax, e);
         }
         if (rank >= r) continue;
         const double sv = d > 0.0 ? sqrt(d) : 0.0;
         s_out[b * s_bs + rank * s_st] = static_cast<float>(sv);
-        const double inv = sv > 0.0 ? 1.0 / sv : 0.0;
+        // Directions 1e-12 below the largest singular value are rounding
+        // noise of the fp32 inputs; their Vh rows are left zero.
+        const double inv = sv > 1e-12 * sqrt(dmax) ? 1.0 / sv : 0.0;
         double* mu = mu_all + static_cast<int64_t>(b) * k * r;
         double* mv = mv_all + static_cast<int64_t>(b) * k * r;
         for (int c = 0; c < k; ++c) {
-            mu[c * r + rank] = v[c * kk + i];
-            mv[c * r + rank] = v[c * kk + i] * inv;
+            mu[c * r + rank] = v[c * ld + i];
+            mv[c * r + rank] = v[c * ld + i] * inv;
         }
     }
 }
@@ -529,24 +660,36 @@ struct ApplyArgs {
 template <typename Acc>
 __global__ void __launch_bounds__(128) panel_apply_kernel(const __grid_constant__ ApplyArgs A) {
     extern __shared__ double smd[];
-    double* sM = smd;                                          // [k][nc]
-    float* sP = reinterpret_cast<float*>(smd + A.k * A.nc);   // [k][128]
+    const int ncp = (A.nc + 15) & ~15;
+    Acc* sM = reinterpret_cast<Acc*>(smd);                  // [k][ncp], zero padded
+    float* sP = reinterpret_cast<float*>(sM + A.k * ncp);  // [k][128]
     const int b = blockIdx.y;
     const int i0 = blockIdx.x * 128;
     const int i = i0 + threadIdx.x;
     const double* M = A.M + b * A.m_bs;
-    for (int idx = threadIdx.x; idx < A.k * A.nc; idx += blockDim.x) sM[idx] = M[idx];
+    for (int idx = threadIdx.x; idx < A.k * ncp; idx += blockDim.x) {
+        const int cp = idx / ncp, c = idx - cp * ncp;
+        sM[idx] = c < A.nc ? static_cast<Acc>(M[cp * A.nc + c]) : Acc(0);
+    }
     const float* P = A.P + b * A.p_bs;
     for (int c = 0; c < A.k; ++c) sP[c * 128 + threadIdx.x] = i < A.L ? P[c * A.p_ld + i] : 0.f;
     __syncthreads();
     if (i >= A.L) return;
     float* o = A.out + b * A.o_bs + i * A.o_si;
-    for (int c = 0; c < A.nc; ++c) {
-        const int lim = A.tri ? min(c + 1, A.k) : A.k;
-        Acc acc = 0;
-        for (int cp = 0; cp < lim; ++cp)
-            acc = fma(static_cast<Acc>(sP[cp * 128 + threadIdx.x]), static_cast<Acc>(sM[cp * A.nc + c]), acc);
-        o[c * A.o_sc] = static_cast<float>(acc);
+    for (int c0 = 0; c0 < A.nc; c0 += 16) {
+        Acc acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = Acc(0);
+        const int lim = A.tri ? min(c0 + 16, A.k) : A.k;
+        for (int cp = 0; cp < lim; ++cp) {
+            const Acc pv = static_cast<Acc>(sP[cp * 128 + threadIdx.x]);
+            const Acc* mrow = sM + cp * ncp + c0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] = fma(pv, mrow[j], acc[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (c0 + j < A.nc) o[(c0 + j) * A.o_sc] = static_cast<float>(acc[j]);
     }
 }
 
@@ -625,7 +768,7 @@ int rsvd_plan(const AdaTensor* a, const AdaTensor* omega, int rank, RsvdPlan* P)
     if (k > kMaxSketch) return fail_msg(ADA_ERR_UNSUPPORTED, "sketch width %lld above %lld", k, kMaxSketch);
     P->k = static_cast<int>(k);
     P->r = rank;
-    P->kp = static_cast<int>((k + 31) / 32 * 32);
+    P->kp = k <= 32 ? 32 : static_cast<int>((k + 15) / 16 * 16);  // MMA N, a multiple of 16
     P->m4 = round4(P->m);
     P->n4 = round4(P->n);
     P->copy_a = !a_tma_ok(a);
@@ -706,12 +849,34 @@ int run_panel_gemm(const RsvdCtx& C, int trans, const float* in, int64_t in_L, i
     G.trans = trans;
     G.status = C.status;
     G.timeout_ns = default_wait_timeout_ns();
-    const dim3 grid(static_cast<unsigned>((G.rows + 127) / 128), static_cast<unsigned>(P.batch));
+    // Work items: enough (batch, tile, K split) items to give every SM two;
+    // the K dimension is split only when the tiles alone are too few.
+    int sms = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        return fail_msg(ADA_ERR_CUDA, "device query failed");
+    G.batch = static_cast<int>(P.batch);
+    G.tiles = (G.rows + 127) / 128;
+    const int nchunks = (G.kdim + 31) / 32;
+    const int64_t tiles_total = static_cast<int64_t>(G.batch) * G.tiles;
+    int splits = 1;
+    if (tiles_total < 2 * sms) splits = static_cast<int>((2 * sms + tiles_total - 1) / tiles_total);
+    if (splits > nchunks) splits = nchunks;
+    G.cps = (nchunks + splits - 1) / splits;
+    G.splits = (nchunks + G.cps - 1) / G.cps;
+    if (G.splits > 1 &&
+        cudaMemsetAsync(out, 0, static_cast<size_t>(P.batch) * P.k * out_ld * sizeof(float), C.s) != cudaSuccess)
+        return fail_msg(ADA_ERR_CUDA, "clearing a panel failed");
+    const int64_t items = tiles_total * G.splits;
+    if (items > (int64_t(1) << 31) - 1) return fail_msg(ADA_ERR_UNSUPPORTED, "too many work items");
+    const dim3 grid(static_cast<unsigned>(items < sms ? items : sms));
     switch (P.kp) {
         case 32: panel_gemm_kernel<32><<<grid, kPgThreads, kPgSmem, C.s>>>(G); break;
+        case 48: panel_gemm_kernel<48><<<grid, kPgThreads, kPgSmem, C.s>>>(G); break;
         case 64: panel_gemm_kernel<64><<<grid, kPgThreads, kPgSmem, C.s>>>(G); break;
+        case 80: panel_gemm_kernel<80><<<grid, kPgThreads, kPgSmem, C.s>>>(G); break;
         case 96: panel_gemm_kernel<96><<<grid, kPgThreads, kPgSmem, C.s>>>(G); break;
-        case 128: panel_gemm_kernel<128><<<grid, kPgThreads, kPgSmem, C.s>>>(G); break;
+        case 112: panel_gemm_kernel<112><<<grid, kPgThreads, kPgSmem, C.s>>>(G); break;
         default: return fail_msg(ADA_ERR_UNSUPPORTED, "panel width %lld", P.kp);
     }
     return cudaGetLastError() == cudaSuccess ? ADA_OK : fail_msg(ADA_ERR_LAUNCH, "panel GEMM launch failed");
@@ -721,8 +886,9 @@ int run_gram(const RsvdCtx& C, const float* panel, int64_t L, int64_t ld, double
     const RsvdPlan& P = *C.P;
     const size_t bytes = static_cast<size_t>(P.batch) * P.k * P.k * 8;
     if (cudaMemsetAsync(g, 0, bytes, C.s) != cudaSuccess) return fail_msg(ADA_ERR_CUDA, "clearing a Gram failed");
-    const size_t smem = static_cast<size_t>(P.k) * (kGramCols + 1) * 4;
-    const dim3 grid(static_cast<unsigned>((L + kGramCols - 1) / kGramCols), static_cast<unsigned>(P.batch));
+    const size_t smem = static_cast<size_t>(P.k) * (kGramCols + 1) * 8;
+    const int64_t per_cta = static_cast<int64_t>(kGramCols) * kGramPasses;
+    const dim3 grid(static_cast<unsigned>((L + per_cta - 1) / per_cta), static_cast<unsigned>(P.batch));
     gram64_kernel<<<grid, 256, smem, C.s>>>(panel, static_cast<int64_t>(P.k) * ld, ld, P.k, static_cast<int>(L), g);
     return cudaGetLastError() == cudaSuccess ? ADA_OK : fail_msg(ADA_ERR_LAUNCH, "Gram launch failed");
 }
@@ -752,7 +918,7 @@ int run_apply(const RsvdCtx& C, const float* panel, int64_t L, int64_t ld, const
     A.o_bs = o_bs;
     A.o_sc = o_sc;
     A.o_si = o_si;
-    const size_t smem = static_cast<size_t>(P.k) * nc * 8 + static_cast<size_t>(P.k) * 128 * 4;
+    const size_t smem = static_cast<size_t>(P.k) * ((nc + 15) & ~15) * sizeof(Acc) + static_cast<size_t>(P.k) * 128 * 4;
     const dim3 grid(static_cast<unsigned>((L + 127) / 128), static_cast<unsigned>(P.batch));
     panel_apply_kernel<Acc><<<grid, 128, smem, C.s>>>(A);
     return cudaGetLastError() == cudaSuccess ? ADA_OK : fail_msg(ADA_ERR_LAUNCH, "panel apply launch failed");
@@ -801,15 +967,16 @@ extern "C" int ada_rsvd(const AdaTensor* a, const AdaTensor* omega, int32_t rank
                         static_cast<long long>(workspace_bytes));
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
         return fail_msg(ADA_ERR_LAYOUT, "workspace must be 256-byte aligned");
-    if ((rc = allow_smem(panel_gemm_kernel<32>, kPgSmem)) || (rc = allow_smem(panel_gemm_kernel<64>, kPgSmem)) ||
-        (rc = allow_smem(panel_gemm_kernel<96>, kPgSmem)) || (rc = allow_smem(panel_gemm_kernel<128>, kPgSmem)) ||
-        (rc = allow_smem(gram64_kernel, static_cast<size_t>(P.k) * (kGramCols + 1) * 4)) ||
+    if ((rc = allow_smem(panel_gemm_kernel<32>, kPgSmem)) || (rc = allow_smem(panel_gemm_kernel<48>, kPgSmem)) ||
+        (rc = allow_smem(panel_gemm_kernel<64>, kPgSmem)) || (rc = allow_smem(panel_gemm_kernel<80>, kPgSmem)) ||
+        (rc = allow_smem(panel_gemm_kernel<96>, kPgSmem)) || (rc = allow_smem(panel_gemm_kernel<112>, kPgSmem)) ||
+        (rc = allow_smem(gram64_kernel, static_cast<size_t>(P.k) * (kGramCols + 1) * 8)) ||
         (rc = allow_smem(chol_inv_kernel, static_cast<size_t>(2) * P.k * P.k * 8)) ||
-        (rc = allow_smem(eig_kernel, static_cast<size_t>(2) * (P.k + 1) * (P.k + 1) * 8)) ||
+        (rc = allow_smem(eig_kernel, static_cast<size_t>(2) * (P.k + 1) * (P.k + 2) * 8)) ||
         (rc = allow_smem(panel_apply_kernel<double>,
-                         static_cast<size_t>(P.k) * P.k * 8 + static_cast<size_t>(P.k) * 128 * 4)) ||
+                         static_cast<size_t>(P.k) * ((P.k + 15) & ~15) * 8 + static_cast<size_t>(P.k) * 128 * 4)) ||
         (rc = allow_smem(panel_apply_kernel<float>,
-                         static_cast<size_t>(P.k) * P.k * 8 + static_cast<size_t>(P.k) * 128 * 4)))
+                         static_cast<size_t>(P.k) * ((P.k + 15) & ~15) * 4 + static_cast<size_t>(P.k) * 128 * 4)))
         return rc;
 
     cudaStream_t strm = static_cast<cudaStream_t>(stream);
@@ -864,9 +1031,9 @@ extern "C" int ada_rsvd(const AdaTensor* a, const AdaTensor* omega, int32_t rank
     if ((rc = run_panel_gemm(C, 1, y, P.m, P.m4, z, P.n4))) return rc;
     // B B^T = W diag(S^2) W^T
     if ((rc = run_gram(C, z, P.n, P.n4, g))) return rc;
-    eig_kernel<<<static_cast<unsigned>(P.batch), kEigThreads, static_cast<size_t>(2) * (P.k + (P.k & 1)) *
-                                                                   (P.k + (P.k & 1)) * 8,
-                 strm>>>(g, P.k, rank, static_cast<float*>(s->data), s->stride[0], s->stride[1], mu, mv, 30);
+    const size_t eig_smem = static_cast<size_t>(2) * (P.k + (P.k & 1)) * (P.k + (P.k & 1) + 1) * 8;
+    eig_kernel<<<static_cast<unsigned>(P.batch), kEigThreads, eig_smem, strm>>>(
+        g, P.k, rank, static_cast<float*>(s->data), s->stride[0], s->stride[1], mu, mv, 30);
     if (cudaGetLastError() != cudaSuccess) return fail_msg(ADA_ERR_LAUNCH, "eigen-solve launch failed");
     // U = Q W[:, :r]; Vh = diag(1/S) W[:, :r]^T B  (low_rank.py:102-107)
     if ((rc = run_apply<float>(C, y, P.m, P.m4, mu, rank, 0, static_cast<float*>(u->data), u->stride[0],
