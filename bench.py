@@ -175,9 +175,10 @@ def run_reference(args, workload):
         "ms_per_step": flops / (value * 1e12) * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1)/sqrt(D) bf16",
-        "config": workload_config(workload, 1),
+        "config": workload_config(workload, args.gpus),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": desc},
+                         "sample": desc + ("; the host cores of one node, so the same value at "
+                                           "every GPU count" if args.gpus > 1 else "")},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "tokens_per_s": workload.tokens / (flops / (value * 1e12)),
