@@ -166,7 +166,9 @@ struct TcLaunch {
     void* out;
     int out_dtype;
     int64_t os[4];
-    int out_vec;      // 1: 16-byte vector stores are aligned
+    int out_vec;      // widest aligned vector store for output rows: 32, 16 or 0 bytes
+    int tma_out;      // 1: the epilogue stages O in the item's Q slot and stores it with `to`
+    CUtensorMap to;   // output [B,H,Nq,dv_out] 16-bit, 64-column x 128-row boxes (tma_out only)
     int round_dtype;  // dtype the reference's result has before its cast back
     float scale_log2; // softmax scale * log2(e)
     int causal;

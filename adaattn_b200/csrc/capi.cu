@@ -350,12 +350,17 @@ int check_mask(const AdaTensor* m, const Plan& P) {
     return ADA_OK;
 }
 
-bool out_vec_ok(const AdaTensor* o) {
+// Widest vector store (16 or 32 bytes) every output row start allows, or 0.
+int out_vec_bytes(const AdaTensor* o) {
     const int eb = elt_bytes(o->dtype);
-    if (o->stride[3] != 1 || !aligned16(o->data)) return false;
-    for (int i = 0; i < 3; ++i)
-        if (((o->stride[i] * eb) % 16) != 0) return false;
-    return true;
+    if (o->stride[3] != 1) return 0;
+    for (int w = 32; w >= 16; w /= 2) {
+        bool ok = (reinterpret_cast<uintptr_t>(o->data) % w) == 0;
+        for (int i = 0; i < 3; ++i)
+            if (((o->stride[i] * eb) % w) != 0) ok = false;
+        if (ok) return w;
+    }
+    return 0;
 }
 
 void copy_strides(int64_t* dst, const AdaTensor* t) {
@@ -609,7 +614,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         L.out = out->data;
         L.out_dtype = out->dtype;
         copy_strides(L.os, out);
-        L.out_vec = out_vec_ok(out) ? 1 : 0;
+        L.out_vec = out_vec_bytes(out);
         L.scale_log2 = params->scale * log2e;
         L.causal = params->causal;
         L.mask = mv;
@@ -647,6 +652,15 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
                     (rc = make_map(&L.tk, ws + P.off16k, dt, 2, L.dqk, P.Nk, P.H, P.B, l, P.Nk * l, P.H * P.Nk * l)) ||
                     (rc = make_map(&L.tv, ws + P.off16v, dt, 2, L.dv, P.Nk, P.H, P.B, lv, P.Nk * lv, P.H * P.Nk * lv)))
                     return rc;
+            }
+            // 16-bit output through TMA stores when every row start is
+            // 16-byte aligned (the epilogue stages the tile in shared memory).
+            if (L.dqk == 128 && L.dv == 128 && (out->dtype == ADA_F16 || out->dtype == ADA_BF16) && out->stride[3] == 1 &&
+                out_vec_bytes(out) >= 16 && P.Nq > 0) {
+                if ((rc = make_map(&L.to, out->data, tma_dtype(out->dtype), 2, P.D, P.Nq, P.H, P.B, out->stride[2],
+                                   out->stride[1], out->stride[0])))
+                    return rc;
+                L.tma_out = 1;
             }
             if ((rc = launch_fmha_tc(L, s))) return fail(rc, "tensor-core attention launch failed (%d,%d)", L.dqk, L.dv);
         }

@@ -215,7 +215,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&bars->q_full[i]), 1);
-            mbar_init(smem_u32(&bars->q_empty[i]), 1);
+            // With a staged epilogue each softmax warpgroup also releases the
+            // Q buffer after its output tile has left it.
+            mbar_init(smem_u32(&bars->q_empty[i]), L.tma_out ? 3 : 1);
             mbar_init(smem_u32(&bars->s_full[i]), 1);
             mbar_init(smem_u32(&bars->p_full[i]), 128);
             mbar_init(smem_u32(&bars->o_full[i]), 1);
@@ -408,11 +410,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
         uint32_t oc = 0;  // items finished by this tile
         bool ok = true;
         uint32_t ic = 0;
+        uint32_t qn = 0;  // items seen: the item's Q buffer is qn & 1
+        const bool leader = (threadIdx.x & 127) == 0;
         int64_t it;
         while (ok && take_item(bars, ic, it, abort_flag, tmo, L.status)) {
             const Item w = decode_item(L, it, n_qtp, nkb);
             const int nt = w.n_t[t];
-            if (nt == 0) continue;
+            const uint32_t qb = qn & 1u;
+            ++qn;
+            if (nt == 0) {
+                if (L.tma_out && leader) mbar_arrive(smem_u32(&bars->q_empty[qb]));
+                continue;
+            }
             const int tile_r0 = (w.qtp * 2 + t) * 128;
             const int qrow = tile_r0 + row;
             const int Nk = static_cast<int>(L.Nk);
@@ -575,7 +584,56 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             const bool row_ok = qrow < L.Nq;
             uint8_t* orow = reinterpret_cast<uint8_t*>(L.out);
             const int64_t obase = w.b * L.os[0] + w.h * L.os[1] + static_cast<int64_t>(qrow) * L.os[2];
+            // The reference's result is rounded to its compute dtype before the
+            // cast to the output dtype; when the two agree the packing below
+            // is that rounding.
+            const bool pre_round = L.round_dtype != L.out_dtype && L.round_dtype != ADA_F32;
             uint32_t r[32];
+            if constexpr (ELT != 2 && DQK == 128 && DV == 128) {
+                if (L.tma_out) {
+                    // Stage the 16-bit tile in this tile's Q slot (no longer read:
+                    // every Q K^T of the item has completed) in the 128-byte
+                    // swizzled box layout, then one thread stores it with TMA.
+                    uint8_t* stg = sQ + qb * C::QBUF_BYTES + t * C::Q_BYTES;
+#pragma unroll
+                    for (int c = 0; c < DV / 32; ++c) {
+                        tmem_ld32(tO + c * 32, r);
+                        tmem_ld_wait();
+                        reg_fence32(r);
+                        uint32_t wv[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            float x0 = __uint_as_float(r[2 * i]) * post, x1 = __uint_as_float(r[2 * i + 1]) * post;
+                            if (pre_round) {
+                                x0 = round_to(x0, L.round_dtype);
+                                x1 = round_to(x1, L.round_dtype);
+                            }
+                            wv[i] = (L.out_dtype == ADA_BF16) ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+                        }
+                        const int atom = (c * 32) / 64;
+                        uint8_t* line = stg + atom * C::BOX + row * 128;
+#pragma unroll
+                        for (int k4 = 0; k4 < 4; ++k4) {
+                            const int chunk = ((c * 32) % 64) / 8 + k4;  // 16-byte chunk within the line
+                            *reinterpret_cast<uint4*>(line + ((chunk ^ (row & 7)) * 16)) =
+                                make_uint4(wv[4 * k4], wv[4 * k4 + 1], wv[4 * k4 + 2], wv[4 * k4 + 3]);
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    if (t == 0)
+                        named_barrier_sync(1, 128);
+                    else
+                        named_barrier_sync(2, 128);
+                    if (leader) {
+                        for (int a = 0; a * 64 < L.dv_out && a < DV / 64; ++a)
+                            tma_store_4d(&L.to, smem_u32(stg + a * C::BOX), a * 64, tile_r0, w.h, w.b);
+                        bulk_commit_group();
+                        bulk_wait_group_read0();
+                        mbar_arrive(smem_u32(&bars->q_empty[qb]));
+                    }
+                    continue;
+                }
+            }
 #pragma unroll
             for (int c = 0; c < DV / 32; ++c) {
                 tmem_ld32(tO + c * 32, r);
@@ -584,25 +642,42 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 if (row_ok) {
                     float o[32];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = round_to(__uint_as_float(r[i]) * post, L.round_dtype);
+                    for (int i = 0; i < 32; ++i) {
+                        const float x = __uint_as_float(r[i]) * post;
+                        o[i] = pre_round ? round_to(x, L.round_dtype) : x;
+                    }
                     const int col0 = c * 32;
                     if (L.out_vec && col0 + 32 <= L.dv_out) {
                         if (L.out_dtype == ADA_F32) {
-                            float4* dst = reinterpret_cast<float4*>(orow + (obase + col0) * 4);
+                            if (L.out_vec == 32) {
 #pragma unroll
-                            for (int i = 0; i < 8; ++i)
-                                dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                                for (int i = 0; i < 4; ++i)
+                                    st_global_v8(orow + (obase + col0 + 8 * i) * 4,
+                                                 reinterpret_cast<const uint32_t*>(o + 8 * i));
+                            } else {
+                                float4* dst = reinterpret_cast<float4*>(orow + (obase + col0) * 4);
+#pragma unroll
+                                for (int i = 0; i < 8; ++i)
+                                    dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                            }
                         } else {
-                            uint4* dst = reinterpret_cast<uint4*>(orow + (obase + col0) * 2);
+                            uint32_t wv[16];
+                            if (L.out_dtype == ADA_BF16) {
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                uint32_t wv[4];
+                                for (int i = 0; i < 16; ++i) wv[i] = pack_bf16x2(o[2 * i], o[2 * i + 1]);
+                            } else {
 #pragma unroll
-                                for (int k2 = 0; k2 < 4; ++k2) {
-                                    const float lo = o[8 * i + 2 * k2], hi = o[8 * i + 2 * k2 + 1];
-                                    wv[k2] = (L.out_dtype == ADA_BF16) ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
-                                }
-                                dst[i] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                                for (int i = 0; i < 16; ++i) wv[i] = pack_f16x2(o[2 * i], o[2 * i + 1]);
+                            }
+                            uint8_t* dst = orow + (obase + col0) * 2;
+                            if (L.out_vec == 32) {
+                                st_global_v8(dst, wv);
+                                st_global_v8(dst + 32, wv + 8);
+                            } else {
+#pragma unroll
+                                for (int i = 0; i < 4; ++i)
+                                    reinterpret_cast<uint4*>(dst)[i] =
+                                        make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
                             }
                         }
                     } else {
@@ -615,6 +690,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
         }
     }
 
+    // Output tiles stored with TMA are complete before the CTA exits.
+    if (L.tma_out && warp < 8 && (threadIdx.x & 127) == 0) bulk_wait_group0();
     tc_fence_before();
     __syncthreads();
     if (warp == 9) {
