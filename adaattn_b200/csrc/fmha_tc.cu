@@ -212,6 +212,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
+    // A launch for a branch and precision that no head chose ends here,
+    // before any setup (the adaptive path launches every variant it may need).
+    if (L.sel.decisions != nullptr) {
+        int any = 0;
+        for (int64_t bh = threadIdx.x; bh < L.B * L.H && !any; bh += blockDim.x) any = head_selected(L.sel, bh);
+        if (!__syncthreads_or(any)) return;
+    }
+
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&bars->q_full[i]), 1);

@@ -70,6 +70,17 @@ __global__ void __launch_bounds__(kProjThreads, 1) proj_tc_kernel(const __grid_c
     const int ntk = static_cast<int>((L.Nk + 127) / 128);
     const int64_t n_items = L.B * L.H * (ntq + ntk);
 
+    // No low-rank head in this launch's precisions: nothing to project.
+    {
+        int any = 0;
+        for (int64_t bh = threadIdx.x; bh < L.B * L.H && !any; bh += blockDim.x) {
+            int prec, low;
+            get_decision(L.dec, bh, &prec, &low);
+            any = low && (((L.tc16_mask | L.fp32_mask) >> prec) & 1u);
+        }
+        if (!__syncthreads_or(any)) return;
+    }
+
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&bars->w_full), 1);
         for (int s = 0; s < kProjStages; ++s) {

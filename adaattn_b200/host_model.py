@@ -75,7 +75,19 @@ class AdaptiveTransformer(nn.Module):
         x = self.embed_dropout(self.token_embedding(input_ids) + self.position_embedding(pos))
         for block in self.blocks:
             x = block(x, attention_mask=attention_mask)
-        return self.head(self.norm(x))
+        return self._logits(self.norm(x))
+
+    def _logits(self, h: torch.Tensor) -> torch.Tensor:
+        """The tied head. A vocabulary that is not a multiple of 64 (50257)
+        sends cuBLAS to a slow unaligned GEMM on the GPU, so the weight is
+        zero-padded to the next multiple of 64 rows and the extra logits are
+        dropped; the values are those of the plain Linear."""
+        w = self.head.weight
+        pad = (-w.shape[0]) % 64
+        if not h.is_cuda or pad == 0:
+            return self.head(h)
+        wp = torch.nn.functional.pad(w, (0, 0, 0, pad))
+        return torch.matmul(h, wp.t())[..., : w.shape[0]].contiguous()
 
     def get_attention_statistics(self):
         stats = []
