@@ -3,10 +3,13 @@
 // with target dtype float32, and the low-rank branch :341-394 on q_low/k_low).
 //
 // A CTA owns 64 query rows of one (b, h); 256 threads as 16 x 16. Key/value
-// blocks of 64 rows are staged in shared memory (K transposed), scores and
-// the online softmax stay in registers, exp is expf (full fp32 accuracy).
+// blocks of 64 rows are staged in shared memory, scores and the online
+// softmax stay in registers, exp is expf (full fp32 accuracy).
 // Thread (ty, tx) owns query rows 4*ty..4*ty+3, score columns tx + 16*i and
-// output columns tx + 16*i: strided ownership keeps shared loads conflict free.
+// output columns 64*g + 4*tx + e. Every operand fetch is a 16-byte shared
+// load (rows padded by 16 bytes, so the 8 rows or 16 keys a warp touches at
+// once fall in distinct banks): Q.K^T takes 8 such loads per 64 FMAs, P.V
+// 4 + 4*G per 64*G FMAs.
 #include "ada_common.cuh"
 #include "ada_internal.h"
 
@@ -15,16 +18,78 @@ namespace {
 
 constexpr int kBQ = 64;
 constexpr int kBK = 64;
-constexpr int kDMax = 128;
 constexpr int kThreadsS = 256;
-constexpr int kLdKt = kBK + 1;
+constexpr int kLdP = kBK + 4;
 
-__global__ void __launch_bounds__(kThreadsS) fmha_simt_kernel(const __grid_constant__ SimtLaunch L) {
+template <int DQKP, int DVP>
+struct SimtCfg {
+    static constexpr int LDQ = DQKP + 4;  // Q and K rows
+    static constexpr int LDV = DVP + 4;
+    static constexpr int G = DVP / 64;    // 4-column output groups per thread
+    static constexpr size_t SMEM =
+        (static_cast<size_t>(2) * kBQ * LDQ + static_cast<size_t>(kBK) * LDV + static_cast<size_t>(kBQ) * kLdP) *
+        sizeof(float);
+};
+
+// rows [row0, row0 + 64) x [0, width) of a [.., N, w] view into a padded
+// shared tile (zeros past n or w); 4 columns per step, 16-byte global loads
+// when the view allows them.
+__device__ __forceinline__ void load_tile(float* dst, int ld, int width_p, const void* src, int dtype,
+                                          int64_t base, int64_t s_row, int64_t s_col, int64_t row0, int64_t n,
+                                          int w, bool vec) {
+    const int groups = width_p / 4;
+    for (int idx = threadIdx.x; idx < kBK * groups; idx += kThreadsS) {
+        const int r = idx / groups, c0 = (idx - r * groups) * 4;
+        const int64_t row = row0 + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < n) {
+            const int64_t e = base + row * s_row + c0 * s_col;
+            if (vec && c0 + 4 <= w) {
+                if (dtype == ADA_F32) {
+                    v = *reinterpret_cast<const float4*>(static_cast<const float*>(src) + e);
+                } else {
+                    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(src) + e);
+                    if (dtype == ADA_BF16) {
+                        const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+                        const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+                        v = make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
+                    } else {
+                        const __half2 lo = *reinterpret_cast<const __half2*>(&u.x);
+                        const __half2 hi = *reinterpret_cast<const __half2*>(&u.y);
+                        v = make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
+                    }
+                }
+            } else {
+                float t[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) t[k] = (c0 + k < w) ? load_as_f32(src, e + k * s_col, dtype) : 0.f;
+                v = make_float4(t[0], t[1], t[2], t[3]);
+            }
+        }
+        *reinterpret_cast<float4*>(dst + r * ld + c0) = v;
+    }
+}
+
+// 16-byte (fp32) or 8-byte (16-bit) vector loads of 4 elements stay aligned.
+__device__ __forceinline__ bool vec_ok(const void* p, int dtype, const int64_t* st) {
+    if (dtype != ADA_F32 && dtype != ADA_F16 && dtype != ADA_BF16) return false;
+    const int eb = dtype == ADA_F32 ? 4 : 2;
+    const int need = 4 * eb;
+    if (st[3] != 1) return false;
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return false;
+    for (int i = 0; i < 3; ++i)
+        if (((st[i] * eb) % need) != 0) return false;
+    return true;
+}
+
+template <int DQKP, int DVP>
+__global__ void __launch_bounds__(kThreadsS, 2) fmha_simt_kernel(const __grid_constant__ SimtLaunch L) {
+    using C = SimtCfg<DQKP, DVP>;
     extern __shared__ float sm[];
-    float* sQ = sm;                          // [kBQ][dqk]
-    float* sKt = sQ + kBQ * kDMax;           // [dqk][kLdKt]
-    float* sV = sKt + kDMax * kLdKt;         // [kBK][dv]
-    float* sP = sV + kBK * kDMax;            // [kBQ][kBK + 1]
+    float* sQ = sm;                     // [kBQ][LDQ]
+    float* sK = sQ + kBQ * C::LDQ;      // [kBK][LDQ]
+    float* sV = sK + kBK * C::LDQ;      // [kBK][LDV]
+    float* sP = sV + kBK * C::LDV;      // [kBQ][kLdP]
 
     const int64_t BH = L.B * L.H;
     const int64_t nqb = (L.Nq + kBQ - 1) / kBQ;
@@ -36,22 +101,18 @@ __global__ void __launch_bounds__(kThreadsS) fmha_simt_kernel(const __grid_const
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
     const int dqk = L.dqk, dv = L.dv;
     const int64_t q0 = qb * kBQ;
+    const bool vq = vec_ok(L.q, L.q_dtype, L.qs);
+    const bool vk = vec_ok(L.k, L.k_dtype, L.ks);
+    const bool vv = vec_ok(L.v, L.v_dtype, L.vs);
 
-    {
-        const int64_t base = b * L.qs[0] + h * L.qs[1];
-        for (int i = tid; i < kBQ * dqk; i += kThreadsS) {
-            const int r = i / dqk, d = i - r * dqk;
-            const int64_t row = q0 + r;
-            sQ[r * dqk + d] = row < L.Nq ? load_as_f32(L.q, base + row * L.qs[2] + d * L.qs[3], L.q_dtype) : 0.f;
-        }
-    }
-    float m[4], l[4], o[4][8];
+    load_tile(sQ, C::LDQ, DQKP, L.q, L.q_dtype, b * L.qs[0] + h * L.qs[1], L.qs[2], L.qs[3], q0, L.Nq, dqk, vq);
+    float m[4], l[4], o[4][4 * C::G];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         m[r] = -INFINITY;
         l[r] = 0.f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) o[r][c] = 0.f;
+        for (int c = 0; c < 4 * C::G; ++c) o[r][c] = 0.f;
     }
     int64_t nkb = (L.Nk + kBK - 1) / kBK;
     if (L.causal) {
@@ -64,32 +125,30 @@ __global__ void __launch_bounds__(kThreadsS) fmha_simt_kernel(const __grid_const
     for (int64_t kb = 0; kb < nkb; ++kb) {
         const int64_t k0 = kb * kBK;
         __syncthreads();
-        for (int i = tid; i < kBK * dqk; i += kThreadsS) {
-            const int r = i / dqk, d = i - r * dqk;
-            const int64_t row = k0 + r;
-            sKt[d * kLdKt + r] = row < L.Nk ? load_as_f32(L.k, kbase + row * L.ks[2] + d * L.ks[3], L.k_dtype) : 0.f;
-        }
-        for (int i = tid; i < kBK * dv; i += kThreadsS) {
-            const int r = i / dv, d = i - r * dv;
-            const int64_t row = k0 + r;
-            sV[r * dv + d] = row < L.Nk ? load_as_f32(L.v, vbase + row * L.vs[2] + d * L.vs[3], L.v_dtype) : 0.f;
-        }
+        load_tile(sK, C::LDQ, DQKP, L.k, L.k_dtype, kbase, L.ks[2], L.ks[3], k0, L.Nk, dqk, vk);
+        load_tile(sV, C::LDV, DVP, L.v, L.v_dtype, vbase, L.vs[2], L.vs[3], k0, L.Nk, dv, vv);
         __syncthreads();
         float s[4][4];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int i = 0; i < 4; ++i) s[r][i] = 0.f;
-        for (int d = 0; d < dqk; ++d) {
-            float a[4], kk[4];
+#pragma unroll 4
+        for (int d = 0; d < DQKP; d += 4) {
+            float4 a[4], kk[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) a[r] = sQ[(ty * 4 + r) * dqk + d];
+            for (int r = 0; r < 4; ++r) a[r] = *reinterpret_cast<const float4*>(sQ + (ty * 4 + r) * C::LDQ + d);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) kk[i] = sKt[d * kLdKt + tx + 16 * i];
+            for (int i = 0; i < 4; ++i) kk[i] = *reinterpret_cast<const float4*>(sK + (tx + 16 * i) * C::LDQ + d);
 #pragma unroll
             for (int r = 0; r < 4; ++r)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) s[r][i] = fmaf(a[r], kk[i], s[r][i]);
+                for (int i = 0; i < 4; ++i) {
+                    s[r][i] = fmaf(a[r].x, kk[i].x, s[r][i]);
+                    s[r][i] = fmaf(a[r].y, kk[i].y, s[r][i]);
+                    s[r][i] = fmaf(a[r].z, kk[i].z, s[r][i]);
+                    s[r][i] = fmaf(a[r].w, kk[i].w, s[r][i]);
+                }
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
@@ -130,21 +189,30 @@ __global__ void __launch_bounds__(kThreadsS) fmha_simt_kernel(const __grid_const
             l[r] = l[r] * alpha + sum;
             m[r] = m_new;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) o[r][c] *= alpha;
+            for (int c = 0; c < 4 * C::G; ++c) o[r][c] *= alpha;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) sP[(ty * 4 + r) * (kBK + 1) + tx + 16 * i] = s[r][i];
+            for (int i = 0; i < 4; ++i) sP[(ty * 4 + r) * kLdP + tx + 16 * i] = s[r][i];
         }
         __syncthreads();
-        for (int c = 0; c < kBK; ++c) {
-            float p[4];
+#pragma unroll 2
+        for (int c = 0; c < kBK; c += 4) {
+            float4 p[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) p[r] = sP[(ty * 4 + r) * (kBK + 1) + c];
+            for (int r = 0; r < 4; ++r) p[r] = *reinterpret_cast<const float4*>(sP + (ty * 4 + r) * kLdP + c);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int col = tx + 16 * j;
-                const float vv = col < dv ? sV[c * dv + col] : 0.f;
+            for (int cc = 0; cc < 4; ++cc) {
 #pragma unroll
-                for (int r = 0; r < 4; ++r) o[r][j] = fmaf(p[r], vv, o[r][j]);
+                for (int g = 0; g < C::G; ++g) {
+                    const float4 v = *reinterpret_cast<const float4*>(sV + (c + cc) * C::LDV + 64 * g + 4 * tx);
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const float pr = cc == 0 ? p[r].x : cc == 1 ? p[r].y : cc == 2 ? p[r].z : p[r].w;
+                        o[r][4 * g + 0] = fmaf(pr, v.x, o[r][4 * g + 0]);
+                        o[r][4 * g + 1] = fmaf(pr, v.y, o[r][4 * g + 1]);
+                        o[r][4 * g + 2] = fmaf(pr, v.z, o[r][4 * g + 2]);
+                        o[r][4 * g + 3] = fmaf(pr, v.w, o[r][4 * g + 3]);
+                    }
+                }
             }
         }
     }
@@ -155,29 +223,40 @@ __global__ void __launch_bounds__(kThreadsS) fmha_simt_kernel(const __grid_const
         if (qrow >= L.Nq) continue;
         const float inv = 1.f / l[r];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int col = tx + 16 * j;
-            if (col < dv) store_from_f32(L.out, obase + qrow * L.os[2] + col * L.os[3], L.out_dtype, o[r][j] * inv);
-        }
+        for (int g = 0; g < C::G; ++g)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int col = 64 * g + 4 * tx + e;
+                if (col < dv)
+                    store_from_f32(L.out, obase + qrow * L.os[2] + col * L.os[3], L.out_dtype, o[r][4 * g + e] * inv);
+            }
     }
 }
 
-}  // namespace
-
-int launch_fmha_simt(const SimtLaunch& L, cudaStream_t stream) {
-    if (L.dqk > kDMax || L.dv > kDMax || L.dqk <= 0 || L.dv <= 0) return ADA_ERR_UNSUPPORTED;
-    const size_t smem = (static_cast<size_t>(kBQ) * kDMax + static_cast<size_t>(kDMax) * kLdKt +
-                         static_cast<size_t>(kBK) * kDMax + static_cast<size_t>(kBQ) * (kBK + 1)) *
-                        sizeof(float);
-    if (cudaFuncSetAttribute(fmha_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
+template <int DQKP, int DVP>
+int launch_simt(const SimtLaunch& L, cudaStream_t stream) {
+    using C = SimtCfg<DQKP, DVP>;
+    auto kern = fmha_simt_kernel<DQKP, DVP>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM)) !=
+        cudaSuccess)
         return ADA_ERR_LAUNCH;
     const int64_t nqb = (L.Nq + kBQ - 1) / kBQ;
     const int64_t grid = nqb * L.B * L.H;
     if (grid <= 0) return ADA_OK;
     if (grid > 0x7fffffffLL) return ADA_ERR_UNSUPPORTED;
-    fmha_simt_kernel<<<static_cast<unsigned>(grid), kThreadsS, smem, stream>>>(L);
+    kern<<<static_cast<unsigned>(grid), kThreadsS, C::SMEM, stream>>>(L);
     return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+}  // namespace
+
+int launch_fmha_simt(const SimtLaunch& L, cudaStream_t stream) {
+    if (L.dqk > 128 || L.dv > 128 || L.dqk <= 0 || L.dv <= 0) return ADA_ERR_UNSUPPORTED;
+    const int qp = L.dqk <= 32 ? 32 : (L.dqk <= 64 ? 64 : 128);
+    const bool v128 = L.dv > 64;
+    if (qp == 32) return v128 ? launch_simt<32, 128>(L, stream) : launch_simt<32, 64>(L, stream);
+    if (qp == 64) return v128 ? launch_simt<64, 128>(L, stream) : launch_simt<64, 64>(L, stream);
+    return v128 ? launch_simt<128, 128>(L, stream) : launch_simt<128, 64>(L, stream);
 }
 
 }  // namespace ada
