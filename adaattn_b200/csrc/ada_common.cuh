@@ -50,12 +50,22 @@ __device__ __forceinline__ void store_from_f32(void* base, int64_t idx, int dtyp
 // Round an fp32 value to the precision of `dtype` (round to nearest even) and
 // return it widened back to fp32: emulates a PyTorch op whose result tensor
 // has that dtype.
+// x rounded (to nearest even) to `dtype` and widened back to fp32, with the
+// single-instruction sm_100 conversions.
 __device__ __forceinline__ float round_to(float x, int dtype) {
-    switch (dtype) {
-        case ADA_F16: return __half2float(__float2half_rn(x));
-        case ADA_BF16: return __bfloat162float(__float2bfloat16_rn(x));
-        default: return x;
+    if (dtype == ADA_BF16) {
+        uint16_t h;
+        asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(x));
+        return __uint_as_float(static_cast<uint32_t>(h) << 16);
     }
+    if (dtype == ADA_F16) {
+        uint16_t h;
+        float r;
+        asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(x));
+        asm("cvt.f32.f16 %0, %1;" : "=f"(r) : "h"(h));
+        return r;
+    }
+    return x;
 }
 
 // ---------------------------------------------------------------------------
@@ -157,7 +167,17 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t sr
         "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most one committed bulk store still reads shared memory.
+__device__ __forceinline__ void bulk_wait_group_read1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // Waits until every committed bulk store has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_group_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -394,13 +414,17 @@ __device__ __forceinline__ void st_global_v8(void* p, const uint32_t* v) {
                  : "memory");
 }
 
+// Two fp32 values -> one packed 16-bit pair (round to nearest even), `lo` in
+// the low half.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
 }
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
-    __half2 v = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
 }
 // Four fp32 values -> four E4M3 bytes (saturating), first value in the low byte.
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {

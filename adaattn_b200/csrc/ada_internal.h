@@ -148,6 +148,10 @@ struct ProjLaunch {
     float* ws32_k;
     unsigned int* status;
     uint64_t timeout_ns;
+    // Output through TMA stores (r_pad 64): 16-bit regions [B*H][N][ld16]
+    // (64-column x 128-row boxes) and fp32 regions [B*H][N][r] (32-column boxes).
+    int tma16, tma32;
+    CUtensorMap to16_q, to16_k, to32_q, to32_k;
 };
 int launch_proj_tc(const ProjLaunch& L, cudaStream_t stream);
 // Vectorised casts for the 16-bit operand region: every tensor of dense heads

@@ -176,6 +176,25 @@ int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int6
     return ADA_OK;
 }
 
+// 3-D map over [batch, rows, width] (innermost first) with a
+// box_cols x 128-row box and 128-byte swizzle; strides in elements.
+int make_map_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int eb, int64_t width, int64_t rows,
+                int64_t batch, int64_t s_row, int64_t s_batch, int box_cols) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int rc = encoder(&enc);
+    if (rc) return rc;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows),
+                          static_cast<cuuint64_t>(batch)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(s_row * eb), static_cast<cuuint64_t>(s_batch * eb)};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), 128, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ADA_ERR_LAYOUT, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return ADA_OK;
+}
+
 CUtensorMapDataType tma_dtype(int dtype) {
     switch (dtype) {
         case ADA_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -583,6 +602,27 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         pj.ws32_k = pl.ws32_k;
         pj.status = st;
         pj.timeout_ns = wait_timeout_ns();
+        // Outputs through TMA stores when the rank pads to 64 columns.
+        if (r_pad == 64 && P.Nq > 0 && P.Nk > 0) {
+            const int64_t BH = P.B * P.H;
+            if (pj.tc16_mask != 0u) {
+                const int64_t l = P.ld16_qk;
+                if ((rc = make_map_3d(&pj.to16_q, pj.ws16_q, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, l, P.Nq, BH, l,
+                                      P.Nq * l, 64)) ||
+                    (rc = make_map_3d(&pj.to16_k, pj.ws16_k, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, l, P.Nk, BH, l,
+                                      P.Nk * l, 64)))
+                    return rc;
+                pj.tma16 = 1;
+            }
+            if (pj.fp32_mask != 0u && (P.r % 4) == 0) {
+                if ((rc = make_map_3d(&pj.to32_q, pj.ws32_q, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, P.r, P.Nq, BH, P.r,
+                                      P.Nq * P.r, 32)) ||
+                    (rc = make_map_3d(&pj.to32_k, pj.ws32_k, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, P.r, P.Nk, BH, P.r,
+                                      P.Nk * P.r, 32)))
+                    return rc;
+                pj.tma32 = 1;
+            }
+        }
         if ((rc = launch_proj_tc(pj, s))) return fail(rc, "tensor-core projection launch failed");
     }
     if (P.need8) {

@@ -252,6 +252,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
     const uint32_t tmem = bars->tmem_base;
     volatile int* abort_flag = &bars->abort_flag;
     const uint64_t tmo = L.timeout_ns;
+    // Launch fields read inside the loops are copied to registers: the asm
+    // memory clobbers of the barrier and tensor-memory wrappers would
+    // otherwise make every use reload them from parameter space.
+    unsigned int* const status = L.status;
 
     if (warp >= 8) {
       regs_decrease<kOtherRegs>();
@@ -270,7 +274,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 const int64_t it = next_item(L, static_next, n_items, n_qtp, nkb);
                 const uint32_t slot = ic & 3u;
                 ok = mbar_wait(smem_u32(&bars->item_empty[slot]), ((ic >> 2) & 1u) ^ 1u, abort_flag, tmo,
-                               L.status);
+                               status);
                 if (!ok) break;
                 static_cast<volatile int64_t*>(bars->item_q)[slot] = it;
                 mbar_arrive(smem_u32(&bars->item_full[slot]));
@@ -278,7 +282,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 if (it < 0) break;
                 const Item w = decode_item(L, it, n_qtp, nkb);
                 const uint32_t qb = qi & 1u;
-                ok = mbar_wait(smem_u32(&bars->q_empty[qb]), ((qi >> 1) & 1u) ^ 1u, abort_flag, tmo, L.status);
+                ok = mbar_wait(smem_u32(&bars->q_empty[qb]), ((qi >> 1) & 1u) ^ 1u, abort_flag, tmo, status);
                 if (!ok) break;
                 const uint32_t qbar = smem_u32(&bars->q_full[qb]);
                 mbar_arrive_expect_tx(qbar, C::QBUF_BYTES);
@@ -291,7 +295,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     for (int half = 0; half < 2; ++half) {
                         const uint32_t st = kvi % C::NSTAGE;
                         const uint32_t ph = (kvi / C::NSTAGE) & 1u;
-                        ok = mbar_wait(smem_u32(&bars->kv_empty[st]), ph ^ 1u, abort_flag, tmo, L.status);
+                        ok = mbar_wait(smem_u32(&bars->kv_empty[st]), ph ^ 1u, abort_flag, tmo, status);
                         if (!ok) break;
                         const uint32_t fbar = smem_u32(&bars->kv_full[st]);
                         uint8_t* dst = sKV + st * C::STAGE_BYTES;
@@ -344,15 +348,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                                       (!first || ks > 0) ? 1u : 0u);
                 }
             };
-            while (ok && take_item(bars, ic, it, abort_flag, tmo, L.status)) {
+            while (ok && take_item(bars, ic, it, abort_flag, tmo, status)) {
                 const Item w = decode_item(L, it, n_qtp, nkb);
                 const uint32_t qb = qi & 1u;
-                ok = mbar_wait(smem_u32(&bars->q_full[qb]), (qi >> 1) & 1u, abort_flag, tmo, L.status);
+                ok = mbar_wait(smem_u32(&bars->q_full[qb]), (qi >> 1) & 1u, abort_flag, tmo, status);
                 if (!ok) break;
                 // K_0 and the first score blocks.
                 {
                     const uint32_t st = kvi % C::NSTAGE;
-                    ok = mbar_wait(smem_u32(&bars->kv_full[st]), (kvi / C::NSTAGE) & 1u, abort_flag, tmo, L.status);
+                    ok = mbar_wait(smem_u32(&bars->kv_full[st]), (kvi / C::NSTAGE) & 1u, abort_flag, tmo, status);
                     if (!ok) break;
                     tc_fence_after();
                     for (int t = 0; t < 2; ++t)
@@ -363,7 +367,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     const uint32_t iv = kvi + 2 * j + 1;
                     const uint32_t sv = iv % C::NSTAGE;
                     ok = mbar_wait(smem_u32(&bars->kv_full[sv]), (iv / C::NSTAGE) & 1u, abort_flag, tmo,
-                                   L.status);
+                                   status);
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t ik = kvi + 2 * j + 2;
@@ -373,7 +377,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     for (int t = 0; t < 2; ++t) {
                         if (!ok) break;
                         if (j < w.n_t[t]) {
-                            ok = mbar_wait(smem_u32(&bars->p_full[t]), pc[t] & 1u, abort_flag, tmo, L.status);
+                            ok = mbar_wait(smem_u32(&bars->p_full[t]), pc[t] & 1u, abort_flag, tmo, status);
                             if (!ok) break;
                             ++pc[t];
                             tc_fence_after();
@@ -383,7 +387,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                         if (j + 1 < w.n_t[t]) {
                             if (!k_ready) {
                                 ok = mbar_wait(smem_u32(&bars->kv_full[sk]), (ik / C::NSTAGE) & 1u,
-                                               abort_flag, tmo, L.status);
+                                               abort_flag, tmo, status);
                                 if (!ok) break;
                                 tc_fence_after();
                                 k_ready = true;
@@ -402,12 +406,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             }
             // Everything issued so far completes before the CTA frees TMEM.
             tc_commit(smem_u32(&bars->teardown));
-            teardown_wait(smem_u32(&bars->teardown), 0, tmo, L.status);
+            teardown_wait(smem_u32(&bars->teardown), 0, tmo, status);
         }
         __syncwarp();
       }
     } else {
         regs_increase<kSoftmaxRegs>();
+        const float scale_log2 = L.scale_log2;
+        const bool causal = L.causal != 0;
+        const void* const mask_data = L.mask.data;
+        const int round_dtype = L.round_dtype, out_dtype = L.out_dtype, out_vec = L.out_vec;
+        const int dv_out = L.dv_out;
+        const bool tma_out = L.tma_out != 0;
         // ---------------- softmax warpgroups ----------------
         const int t = warp >> 2;
         const int row = (warp & 3) * 32 + lane;  // TMEM lane == row of the tile
@@ -421,13 +431,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
         uint32_t qn = 0;  // items seen: the item's Q buffer is qn & 1
         const bool leader = (threadIdx.x & 127) == 0;
         int64_t it;
-        while (ok && take_item(bars, ic, it, abort_flag, tmo, L.status)) {
+        while (ok && take_item(bars, ic, it, abort_flag, tmo, status)) {
             const Item w = decode_item(L, it, n_qtp, nkb);
             const int nt = w.n_t[t];
             const uint32_t qb = qn & 1u;
             ++qn;
             if (nt == 0) {
-                if (L.tma_out && leader) mbar_arrive(smem_u32(&bars->q_empty[qb]));
+                if (tma_out && leader) mbar_arrive(smem_u32(&bars->q_empty[qb]));
                 continue;
             }
             const int tile_r0 = (w.qtp * 2 + t) * 128;
@@ -438,7 +448,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             float m_run = -INFINITY;
             float l_run = 0.f;
             for (int j = 0; j < nt; ++j) {
-                ok = mbar_wait(smem_u32(&bars->s_full[t]), sc & 1u, abort_flag, tmo, L.status);
+                ok = mbar_wait(smem_u32(&bars->s_full[t]), sc & 1u, abort_flag, tmo, status);
                 if (!ok) break;
                 ++sc;
                 tc_fence_after();
@@ -462,19 +472,19 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                         s[96 + i] = __uint_as_float(r3[i]);
                     }
                 }
-                float sl2 = L.scale_log2;
+                float sl2 = scale_log2;
                 if constexpr (ELT == 2) sl2 *= sq * L.k_scale[w.bh * L.nt_k + j];
                 const int kv0 = j * 128;
-                const bool edge = (kv0 + 128 > Nk) || (L.causal && kv0 + 127 > tile_r0);
+                const bool edge = (kv0 + 128 > Nk) || (causal && kv0 + 127 > tile_r0);
                 if (edge) {
                     const int lim_k = Nk - kv0;                                   // keys >= Nk
-                    const int lim_c = L.causal ? (qrow - kv0 + 1) : 128;          // keys > qrow
+                    const int lim_c = causal ? (qrow - kv0 + 1) : 128;          // keys > qrow
                     const int lim = lim_k < lim_c ? lim_k : lim_c;
 #pragma unroll
                     for (int c = 0; c < 128; ++c)
                         if (c >= lim) s[c] = -INFINITY;
                 }
-                if (L.mask.data != nullptr && qrow < L.Nq) {
+                if (mask_data != nullptr && qrow < L.Nq) {
                     // logits are s * scale + m; in raw-score units that is s + m / scale.
                     const float inv_scale = 1.f / (sl2 * 0.69314718056f);
                     const int64_t mb = w.b * L.mask.s[0] + w.h * L.mask.s[1] + qrow * L.mask.s[2];
@@ -482,11 +492,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     for (int c = 0; c < 128; ++c) {
                         const int kv = kv0 + c;
                         if (kv < Nk) {
-                            const float mv = load_as_f32(L.mask.data, mb + kv * L.mask.s[3], L.mask.dtype);
+                            const float mv = load_as_f32(mask_data, mb + kv * L.mask.s[3], L.mask.dtype);
                             if (L.mask.dtype == ADA_BOOL) {
                                 if (mv == 0.f) s[c] = -INFINITY;
                             } else {
-                                s[c] += round_to(mv, L.round_dtype) * inv_scale;
+                                s[c] += round_to(mv, round_dtype) * inv_scale;
                             }
                         }
                     }
@@ -582,7 +592,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 mbar_arrive(smem_u32(&bars->p_full[t]));
             }
             if (!ok) break;
-            ok = mbar_wait(smem_u32(&bars->o_full[t]), oc & 1u, abort_flag, tmo, L.status);
+            ok = mbar_wait(smem_u32(&bars->o_full[t]), oc & 1u, abort_flag, tmo, status);
             if (!ok) break;
             ++oc;
             tc_fence_after();
@@ -595,10 +605,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             // The reference's result is rounded to its compute dtype before the
             // cast to the output dtype; when the two agree the packing below
             // is that rounding.
-            const bool pre_round = L.round_dtype != L.out_dtype && L.round_dtype != ADA_F32;
+            const bool pre_round = round_dtype != out_dtype && round_dtype != ADA_F32;
             uint32_t r[32];
             if constexpr (ELT != 2 && DQK == 128 && DV == 128) {
-                if (L.tma_out) {
+                if (tma_out) {
                     // Stage the 16-bit tile in this tile's Q slot (no longer read:
                     // every Q K^T of the item has completed) in the 128-byte
                     // swizzled box layout, then one thread stores it with TMA.
@@ -613,10 +623,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                         for (int i = 0; i < 16; ++i) {
                             float x0 = __uint_as_float(r[2 * i]) * post, x1 = __uint_as_float(r[2 * i + 1]) * post;
                             if (pre_round) {
-                                x0 = round_to(x0, L.round_dtype);
-                                x1 = round_to(x1, L.round_dtype);
+                                x0 = round_to(x0, round_dtype);
+                                x1 = round_to(x1, round_dtype);
                             }
-                            wv[i] = (L.out_dtype == ADA_BF16) ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+                            wv[i] = (out_dtype == ADA_BF16) ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
                         }
                         const int atom = (c * 32) / 64;
                         uint8_t* line = stg + atom * C::BOX + row * 128;
@@ -633,7 +643,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     else
                         named_barrier_sync(2, 128);
                     if (leader) {
-                        for (int a = 0; a * 64 < L.dv_out && a < DV / 64; ++a)
+                        for (int a = 0; a * 64 < dv_out && a < DV / 64; ++a)
                             tma_store_4d(&L.to, smem_u32(stg + a * C::BOX), a * 64, tile_r0, w.h, w.b);
                         bulk_commit_group();
                         bulk_wait_group_read0();
@@ -652,12 +662,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const float x = __uint_as_float(r[i]) * post;
-                        o[i] = pre_round ? round_to(x, L.round_dtype) : x;
+                        o[i] = pre_round ? round_to(x, round_dtype) : x;
                     }
                     const int col0 = c * 32;
-                    if (L.out_vec && col0 + 32 <= L.dv_out) {
-                        if (L.out_dtype == ADA_F32) {
-                            if (L.out_vec == 32) {
+                    if (out_vec && col0 + 32 <= dv_out) {
+                        if (out_dtype == ADA_F32) {
+                            if (out_vec == 32) {
 #pragma unroll
                                 for (int i = 0; i < 4; ++i)
                                     st_global_v8(orow + (obase + col0 + 8 * i) * 4,
@@ -670,7 +680,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                             }
                         } else {
                             uint32_t wv[16];
-                            if (L.out_dtype == ADA_BF16) {
+                            if (out_dtype == ADA_BF16) {
 #pragma unroll
                                 for (int i = 0; i < 16; ++i) wv[i] = pack_bf16x2(o[2 * i], o[2 * i + 1]);
                             } else {
@@ -678,7 +688,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                                 for (int i = 0; i < 16; ++i) wv[i] = pack_f16x2(o[2 * i], o[2 * i + 1]);
                             }
                             uint8_t* dst = orow + (obase + col0) * 2;
-                            if (L.out_vec == 32) {
+                            if (out_vec == 32) {
                                 st_global_v8(dst, wv);
                                 st_global_v8(dst + 32, wv + 8);
                             } else {
@@ -690,8 +700,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                         }
                     } else {
                         for (int i = 0; i < 32; ++i)
-                            if (col0 + i < L.dv_out)
-                                store_from_f32(L.out, obase + (col0 + i) * L.os[3], L.out_dtype, o[i]);
+                            if (col0 + i < dv_out)
+                                store_from_f32(L.out, obase + (col0 + i) * L.os[3], out_dtype, o[i]);
                     }
                 }
             }

@@ -19,6 +19,7 @@ namespace {
 
 constexpr int kProjThreads = 256;
 constexpr int kProjStages = 4;
+constexpr int kStageBytes = 32 * 1024;  // one staged 128 x 64 output tile (fp32)
 
 struct __align__(8) ProjBarriers {
     uint64_t w_full;
@@ -61,7 +62,8 @@ __global__ void __launch_bounds__(kProjThreads, 1) proj_tc_kernel(const __grid_c
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sW = base;
     uint8_t* sX = base + W_BYTES;
-    ProjBarriers* bars = reinterpret_cast<ProjBarriers*>(sX + kProjStages * X_BYTES);
+    uint8_t* sStage = sX + kProjStages * X_BYTES;  // [2][32 KB] output staging (RP 64)
+    ProjBarriers* bars = reinterpret_cast<ProjBarriers*>(sStage + (RP == 64 ? 2 * kStageBytes : 0));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t fmt = L.in_dtype == ADA_BF16 ? 1u : 0u;
     const uint32_t idesc = IDESC | (fmt << 7) | (fmt << 10);
@@ -174,8 +176,10 @@ __global__ void __launch_bounds__(kProjThreads, 1) proj_tc_kernel(const __grid_c
         }
         __syncwarp();
     } else if (warp >= 4) {
+        const int r_reg = L.r, in_dtype_reg = L.in_dtype;
         const int row = (warp & 3) * 32 + lane;
         const uint32_t lane_bits = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const bool leader = threadIdx.x == 128;
         uint32_t xi = 0;
         bool ok = true;
         for (int64_t it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
@@ -198,20 +202,70 @@ __global__ void __launch_bounds__(kProjThreads, 1) proj_tc_kernel(const __grid_c
             }
             tc_fence_before();
             mbar_arrive(smem_u32(&bars->acc_empty[ab]));
-            ++xi;
+            const uint32_t item_no = xi++;
             const int64_t nrows = w.which == 0 ? L.Nq : L.Nk;
             const int64_t grow = static_cast<int64_t>(w.tile) * 128 + row;
-            if (grow >= nrows) continue;
-            // The reference's Linear returns the inputs' dtype.
+            // The reference's Linear returns the inputs' dtype. (Launch
+            // fields are copied to registers first: the asm memory clobbers
+            // above would otherwise make the loop reload them each step.)
+            const int rr = r_reg, in_dt = in_dtype_reg;
 #pragma unroll
-            for (int i = 0; i < RP; ++i) y[i] = i < L.r ? round_to(y[i], L.in_dtype) : 0.f;
-            if ((L.fp32_mask >> prec) & 1u) {
+            for (int i = 0; i < RP; ++i) y[i] = i < rr ? round_to(y[i], in_dt) : 0.f;
+            const bool to32 = (L.fp32_mask >> prec) & 1u;
+            const bool f16 = (L.f16_mask >> prec) & 1u;
+            if constexpr (RP == 64) {
+                if (to32 ? L.tma32 : L.tma16) {
+                    // Stage the 128-row tile in the swizzled box layout and let
+                    // one thread store it with TMA (rows past N are clipped).
+                    uint8_t* stg = sStage + (item_no & 1u) * kStageBytes;
+                    if (leader) bulk_wait_group_read1();  // the store from this buffer two items ago
+                    named_barrier_sync(1, 128);
+                    if (to32) {
+#pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            uint8_t* line = stg + k * (128 * 128) + row * 128;
+#pragma unroll
+                            for (int c = 0; c < 8; ++c)
+                                *reinterpret_cast<float4*>(line + ((c ^ (row & 7)) * 16)) =
+                                    make_float4(y[k * 32 + 4 * c], y[k * 32 + 4 * c + 1], y[k * 32 + 4 * c + 2],
+                                                y[k * 32 + 4 * c + 3]);
+                        }
+                    } else {
+                        uint8_t* line = stg + row * 128;
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) {
+                            uint32_t p[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float lo = y[8 * c + 2 * e], hi = y[8 * c + 2 * e + 1];
+                                p[e] = f16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
+                            }
+                            *reinterpret_cast<uint4*>(line + ((c ^ (row & 7)) * 16)) = make_uint4(p[0], p[1], p[2], p[3]);
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    named_barrier_sync(1, 128);
+                    if (leader) {
+                        const int bh = static_cast<int>(w.bh);
+                        if (to32) {
+                            const CUtensorMap* map = w.which == 0 ? &L.to32_q : &L.to32_k;
+                            for (int k = 0; k < 2 && k * 32 < L.r; ++k)
+                                tma_store_3d(map, smem_u32(stg + k * (128 * 128)), k * 32, w.tile * 128, bh);
+                        } else {
+                            tma_store_3d(w.which == 0 ? &L.to16_q : &L.to16_k, smem_u32(stg), 0, w.tile * 128, bh);
+                        }
+                        bulk_commit_group();
+                    }
+                    continue;
+                }
+            }
+            if (grow >= nrows) continue;
+            if (to32) {
                 float* out = (w.which == 0 ? L.ws32_q : L.ws32_k) + (w.bh * nrows + grow) * L.r;
 #pragma unroll
                 for (int i = 0; i < RP; ++i)
                     if (i < L.r) out[i] = y[i];
             } else {
-                const bool f16 = (L.f16_mask >> prec) & 1u;
                 uint16_t* out = reinterpret_cast<uint16_t*>(w.which == 0 ? L.ws16_q : L.ws16_k) +
                                 (w.bh * nrows + grow) * L.ld16;
                 uint4* dst = reinterpret_cast<uint4*>(out);
@@ -227,6 +281,7 @@ __global__ void __launch_bounds__(kProjThreads, 1) proj_tc_kernel(const __grid_c
                 }
             }
         }
+        if (leader) bulk_wait_group0();
     }
 
     tc_fence_before();
@@ -239,7 +294,7 @@ __global__ void __launch_bounds__(kProjThreads, 1) proj_tc_kernel(const __grid_c
 
 template <int D, int RP>
 int launch_proj(const ProjLaunch& L, cudaStream_t stream) {
-    constexpr int smem = RP * D * 2 + kProjStages * 128 * D * 2 + 1024 + 256;
+    constexpr int smem = RP * D * 2 + kProjStages * 128 * D * 2 + (RP == 64 ? 2 * kStageBytes : 0) + 1024 + 256;
     auto kern = proj_tc_kernel<D, RP>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return ADA_ERR_LAUNCH;
