@@ -128,6 +128,7 @@ struct PrepLaunch {
     float* scale_k; // [B,H,nt_k]
     float* scale_v; // [B,H]
     int64_t nt_q, nt_k;
+    int low_src16;  // 1: low-rank q_low/k_low are already in the 16-bit region (input dtype)
 };
 int launch_prep16(const PrepLaunch& L, cudaStream_t stream);
 
@@ -141,6 +142,7 @@ struct ProjLaunch {
     int64_t B, H, Nq, Nk;
     int D, r, r_pad;
     uint32_t tc16_mask, f16_mask, fp32_mask;
+    uint32_t fp8_mask;  // E4M3 heads: q_low/k_low go to the 16-bit region in the input dtype
     void* ws16_q;
     void* ws16_k;
     int64_t ld16;

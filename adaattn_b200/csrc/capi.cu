@@ -220,6 +220,7 @@ struct Plan {
     int dqk_dense, dqk_low, dv_pad;
     int64_t ld16_qk, ld16_v;
     bool need16, need32, need8;
+    bool proj_tc_shape;  // low-rank projection can run on the tensor cores
     int64_t nt_q, nt_k;
     size_t off16q, off16k, off16v, off32q, off32k, off8q, off8k, off8v;
     size_t off_amax_q, off_amax_k, off_amax_v, off_sq, off_sk, off_sv;
@@ -304,6 +305,11 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
     }
     P->need32 = ((P->possible & P->fp32_mask) != 0) && P->low_possible;
     P->need8 = (P->possible & P->fp8_mask) != 0;
+    // E4M3 low-rank heads take their projection from the tensor-core kernel,
+    // which writes q_low/k_low into the 16-bit region.
+    P->proj_tc_shape = P->low_possible && P->direct_ok &&
+                       ((P->D == 128 && P->r <= 128) || (P->D == 64 && P->r <= 64));
+    if (P->need8 && P->proj_tc_shape) P->need16 = true;
     P->nt_q = (P->Nq + 127) / 128;
     P->nt_k = (P->Nk + 127) / 128;
     const int64_t BH = P->B * P->H;
@@ -556,9 +562,8 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
     // Low-rank q/k projection on the tensor cores when the inputs are 16-bit
     // and TMA-readable; the SIMT projection kernels cover every other case.
     const int r_pad = P.low_possible ? pad_width(P.r) : 0;
-    const bool proj_tc = P.low_possible && (P.need16 || P.need32) && P.direct_ok &&
-                         (reinterpret_cast<uintptr_t>(w_down->data) & 15u) == 0 &&
-                         ((P.D == 128 && (r_pad == 64 || r_pad == 128)) || (P.D == 64 && r_pad == 64));
+    const bool proj_tc = P.proj_tc_shape && (P.need16 || P.need32) &&
+                         (reinterpret_cast<uintptr_t>(w_down->data) & 15u) == 0;
     if (P.need16) {
         pl.ws16_q = ws + P.off16q;
         pl.ws16_k = ws + P.off16k;
@@ -593,6 +598,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         pj.r_pad = r_pad;
         // Only precisions whose operand region exists are written.
         pj.tc16_mask = P.need16 ? (P.tc16_mask & P.possible) : 0u;
+        pj.fp8_mask = P.need8 ? (P.fp8_mask & P.possible) : 0u;
         pj.f16_mask = P.f16_mask;
         pj.fp32_mask = P.need32 ? (P.fp32_mask & P.possible) : 0u;
         pj.ws16_q = pl.ws16_q;
@@ -605,7 +611,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         // Outputs through TMA stores when the rank pads to 64 columns.
         if (r_pad == 64 && P.Nq > 0 && P.Nk > 0) {
             const int64_t BH = P.B * P.H;
-            if (pj.tc16_mask != 0u) {
+            if ((pj.tc16_mask | pj.fp8_mask) != 0u) {
                 const int64_t l = P.ld16_qk;
                 if ((rc = make_map_3d(&pj.to16_q, pj.ws16_q, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, l, P.Nq, BH, l,
                                       P.Nq * l, 64)) ||
@@ -635,6 +641,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         pl.scale_q = reinterpret_cast<float*>(ws + P.off_sq);
         pl.scale_k = reinterpret_cast<float*>(ws + P.off_sk);
         pl.scale_v = reinterpret_cast<float*>(ws + P.off_sv);
+        pl.low_src16 = proj_tc ? 1 : 0;
         if ((rc = launch_prep8(pl, s))) return fail(rc, "prep8 launch failed");
     }
 

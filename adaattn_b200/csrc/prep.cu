@@ -253,9 +253,12 @@ __global__ void __launch_bounds__(kThreads) prep8_kernel(const __grid_constant__
     const int r = static_cast<int>(L.r);
     const int64_t tile = blockIdx.x;
     if (threadIdx.x < 3) s_amax[threadIdx.x] = 0u;
+    // low_src16: q_low/k_low already sit in the 16-bit region (written by the
+    // tensor-core projection in the inputs' dtype); no projection here.
+    const bool src16 = low && L.low_src16;
     float* w_t = sm;
-    float* sx = sm + (low ? D * r : 0);
-    if (low) stage_weight(L, w_t);
+    float* sx = sm + ((low && !src16) ? D * r : 0);
+    if (low && !src16) stage_weight(L, w_t);
     if (pass == 1 && threadIdx.x == 0) {
         float sq = 1.f, sk = 1.f, svv = 0.f;
         if (tile < L.nt_q) {
@@ -282,9 +285,19 @@ __global__ void __launch_bounds__(kThreads) prep8_kernel(const __grid_constant__
         if (tile >= nt) continue;
         const void* x = which == 0 ? L.q : (which == 1 ? L.k : L.v);
         const int64_t* st = which == 0 ? L.qs : (which == 1 ? L.ks : L.vs);
+        int64_t st16[4];
+        if (src16 && which < 2) {
+            // [B*H][N][ld16] plane of this head, read from its own base
+            x = reinterpret_cast<const uint16_t*>(which == 0 ? L.ws16_q : L.ws16_k) + bh * nrows * L.ld16_qk;
+            st16[0] = 0;
+            st16[1] = 0;
+            st16[2] = L.ld16_qk;
+            st16[3] = 1;
+            st = st16;
+        }
         uint8_t* dst8 = which == 0 ? L.ws8_q : (which == 1 ? L.ws8_k : L.ws8_v);
-        const bool proj = low && which < 2;
-        const int width = proj ? r : D;
+        const bool proj = low && which < 2 && !src16;
+        const int width = (low && which < 2) ? r : D;
         float amax = 0.f;
         for (int half = 0; half < 2; ++half) {
             const int64_t row0 = tile * 128 + half * kRows;
@@ -395,7 +408,7 @@ int launch_prep32(const PrepLaunch& L, cudaStream_t stream) {
 int launch_prep8(const PrepLaunch& L, cudaStream_t stream) {
     const int64_t nt = L.nt_q > L.nt_k ? L.nt_q : L.nt_k;
     if (nt == 0 || L.B * L.H == 0) return ADA_OK;
-    const size_t smem = proj_smem(L, L.w_down != nullptr);
+    const size_t smem = proj_smem(L, L.w_down != nullptr && !L.low_src16);
     if (set_smem(prep8_kernel, smem) != ADA_OK) return ADA_ERR_LAUNCH;
     const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H));
     prep8_kernel<<<grid, kThreads, smem, stream>>>(L, 0);
