@@ -68,6 +68,8 @@ DENSE_CASES = [
     (torch.float32, O.FP32, 32, 77, 140),
     (torch.float32, O.FP16, 96, 100, 100),     # head dim padded to 128
     (torch.bfloat16, O.BF16, 32, 150, 150),    # head dim padded to 64
+    (torch.float32, O.FP32, 128, 100, 300),    # pipelined CUDA-core path, fp32 K and V
+    (torch.float32, O.FP32, 72, 90, 90),       # pipelined, zero-filled columns 72..127
 ]
 
 
@@ -95,6 +97,8 @@ LOW_CASES = [
     (torch.bfloat16, O.FP16, 128, 100, 190),
     (torch.float16, O.FP32, 128, 64, 140),
     (torch.bfloat16, O.BF16, 64, 100, 128),    # r_pad 128 > D: SIMT projection
+    (torch.bfloat16, O.FP32, 128, 100, 150),   # pipelined CUDA-core path, bf16 V
+    (torch.float32, O.FP32, 128, 30, 100),     # rank not a multiple of 4: unpipelined path
 ]
 
 
