@@ -328,6 +328,14 @@ __device__ __forceinline__ void reg_fence16(uint32_t (&r)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i])::"memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -425,6 +433,12 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     uint32_t d;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
     return d;
+}
+// The two fp16 halves of a packed pair as fp32 (low half first); exact.
+__device__ __forceinline__ void unpack_f16x2(uint32_t v, float& lo, float& hi) {
+    asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(v));
 }
 // Four fp32 values -> four E4M3 bytes (saturating), first value in the low byte.
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {

@@ -129,6 +129,17 @@ struct PrepLaunch {
     float* scale_v; // [B,H]
     int64_t nt_q, nt_k;
     int low_src16;  // 1: low-rank q_low/k_low are already in the 16-bit region (input dtype)
+    // FP32 low-rank heads of 16-bit inputs on the tensor cores: q_low/k_low
+    // (fp32 region, values of the inputs' dtype) and v scaled by powers of
+    // two into fp16: q, k [B*H][N][64], v [B*H][N][128].
+    uint32_t split_mask;      // precision codes served this way (FP32) or 0
+    uint16_t* wss_q;
+    uint16_t* wss_k;
+    uint16_t* wss_v;
+    float* split_sq;          // [B,H,nt_q] power-of-two scales of q_low tiles
+    float* split_sk;          // [B,H,nt_k]
+    float* split_sv;          // [B,H]
+    unsigned int* split_amax_v;  // [B,H] max |v| bits, zeroed before launch_split
 };
 int launch_prep16(const PrepLaunch& L, cudaStream_t stream);
 
@@ -161,11 +172,12 @@ int launch_proj_tc(const ProjLaunch& L, cudaStream_t stream);
 int launch_cast16(const PrepLaunch& L, int skip_low_rank_qk, cudaStream_t stream);
 int launch_prep32(const PrepLaunch& L, cudaStream_t stream);
 int launch_prep8(const PrepLaunch& L, cudaStream_t stream);
+int launch_split(const PrepLaunch& L, cudaStream_t stream);
 
 // --- tensor-core FMHA (tcgen05) -----------------------------------------------
 struct TcLaunch {
     CUtensorMap tq, tk, tv;
-    int elt;          // 0 f16, 1 bf16, 2 e4m3
+    int elt;          // 0 f16, 1 bf16, 2 e4m3, 3 fp32 heads: scaled fp16 operands, P as fp16 hi + lo
     int dqk, dv;      // operand widths (64 or 128)
     int64_t B, H, Nq, Nk;
     int dv_out;       // real value width stored
@@ -180,9 +192,9 @@ struct TcLaunch {
     int causal;
     MaskView mask;
     HeadSelect sel;
-    const float* q_scale;  // e4m3: [B,H,nt_q]
-    const float* k_scale;  // e4m3: [B,H,nt_k]
-    const float* v_scale;  // e4m3: [B,H]
+    const float* q_scale;  // e4m3 and split: [B,H,nt_q]
+    const float* k_scale;  // e4m3 and split: [B,H,nt_k]
+    const float* v_scale;  // e4m3 and split: [B,H]
     int64_t nt_q, nt_k;
     int* work_counter;  // zeroed work-item counter (dynamic scheduling), or nullptr (static striding)
     unsigned int* status;

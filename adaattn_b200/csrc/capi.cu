@@ -220,10 +220,12 @@ struct Plan {
     int dqk_dense, dqk_low, dv_pad;
     int64_t ld16_qk, ld16_v;
     bool need16, need32, need8;
+    bool split;          // FP32 low-rank heads on the tensor cores as split fp16 operands
     bool proj_tc_shape;  // low-rank projection can run on the tensor cores
     int64_t nt_q, nt_k;
     size_t off16q, off16k, off16v, off32q, off32k, off8q, off8k, off8v;
     size_t off_amax_q, off_amax_k, off_amax_v, off_sq, off_sk, off_sv;
+    size_t offs_q, offs_k, offs_v, offs_sq, offs_sk, offs_sv, offs_amax;
     size_t required;      // bytes the operand regions need
     size_t off_counters;  // work-item counters of the tensor-core launches
     size_t total;         // required + counters
@@ -305,6 +307,10 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
     }
     P->need32 = ((P->possible & P->fp32_mask) != 0) && P->low_possible;
     P->need8 = (P->possible & P->fp8_mask) != 0;
+    // FP32 low-rank heads of 16-bit inputs with r <= 64: fp32-accurate on the
+    // tensor cores (split fp16 operands); dense FP32 heads, wider ranks and
+    // fp32 inputs stay on the CUDA cores.
+    P->split = P->need32 && P->r <= 64 && (P->in_dtype == ADA_F16 || P->in_dtype == ADA_BF16);
     // E4M3 low-rank heads take their projection from the tensor-core kernel,
     // which writes q_low/k_low into the 16-bit region.
     P->proj_tc_shape = P->low_possible && P->direct_ok &&
@@ -327,6 +333,22 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
         off = align256(off + static_cast<size_t>(BH * P->Nq * P->r) * 4);
         P->off32k = off;
         off = align256(off + static_cast<size_t>(BH * P->Nk * P->r) * 4);
+    }
+    if (P->split) {
+        P->offs_q = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nq * 64) * 2);
+        P->offs_k = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nk * 64) * 2);
+        P->offs_v = off;
+        off = align256(off + static_cast<size_t>(BH * P->Nk * 128) * 2);
+        P->offs_sq = off;
+        off = align256(off + static_cast<size_t>(BH * P->nt_q) * 4);
+        P->offs_sk = off;
+        off = align256(off + static_cast<size_t>(BH * P->nt_k) * 4);
+        P->offs_sv = off;
+        off = align256(off + static_cast<size_t>(BH) * 4);
+        P->offs_amax = off;
+        off = align256(off + static_cast<size_t>(BH) * 4);
     }
     if (P->need8) {
         P->off8q = off;
@@ -645,6 +667,20 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         if ((rc = launch_prep8(pl, s))) return fail(rc, "prep8 launch failed");
     }
 
+    if (P.split) {
+        pl.split_mask = P.fp32_mask;
+        pl.wss_q = reinterpret_cast<uint16_t*>(ws + P.offs_q);
+        pl.wss_k = reinterpret_cast<uint16_t*>(ws + P.offs_k);
+        pl.wss_v = reinterpret_cast<uint16_t*>(ws + P.offs_v);
+        pl.split_sq = reinterpret_cast<float*>(ws + P.offs_sq);
+        pl.split_sk = reinterpret_cast<float*>(ws + P.offs_sk);
+        pl.split_sv = reinterpret_cast<float*>(ws + P.offs_sv);
+        pl.split_amax_v = reinterpret_cast<unsigned int*>(ws + P.offs_amax);
+        if (cudaMemsetAsync(pl.split_amax_v, 0, static_cast<size_t>(P.B * P.H) * 4, s) != cudaSuccess)
+            return fail(ADA_ERR_CUDA, "clearing the split amax failed");
+        if ((rc = launch_split(pl, s))) return fail(rc, "split operand launch failed");
+    }
+
     // ---- tensor-core launches ---------------------------------------------
     const float log2e = 1.4426950408889634f;
     int* counters = have_ws ? reinterpret_cast<int*>(ws + P.off_counters) : nullptr;
@@ -733,10 +769,28 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
             if ((rc = launch_fmha_tc(L, s))) return fail(rc, "E4M3 attention launch failed");
         }
     }
+    if (P.split) {
+        TcLaunch L;
+        base_tc(L);
+        L.elt = 3;
+        L.round_dtype = ADA_F32;
+        L.sel = HeadSelect{decisions, P.fp32_mask, 1};
+        L.dqk = 64;
+        L.dv = 128;
+        L.q_scale = reinterpret_cast<float*>(ws + P.offs_sq);
+        L.k_scale = reinterpret_cast<float*>(ws + P.offs_sk);
+        L.v_scale = reinterpret_cast<float*>(ws + P.offs_sv);
+        const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        if ((rc = make_map(&L.tq, ws + P.offs_q, dt, 2, 64, P.Nq, P.H, P.B, 64, P.Nq * 64, P.H * P.Nq * 64)) ||
+            (rc = make_map(&L.tk, ws + P.offs_k, dt, 2, 64, P.Nk, P.H, P.B, 64, P.Nk * 64, P.H * P.Nk * 64)) ||
+            (rc = make_map(&L.tv, ws + P.offs_v, dt, 2, 128, P.Nk, P.H, P.B, 128, P.Nk * 128, P.H * P.Nk * 128)))
+            return rc;
+        if ((rc = launch_fmha_tc(L, s))) return fail(rc, "split fp32 attention launch failed");
+    }
     // ---- fp32 heads on the CUDA cores ---------------------------------------
     if (P.possible & P.fp32_mask) {
         for (int low = 0; low < 2; ++low) {
-            if (low ? !P.low_possible : !P.dense_possible) continue;
+            if (low ? (!P.low_possible || P.split) : !P.dense_possible) continue;
             SimtLaunch L{};
             L.B = P.B;
             L.H = P.H;

@@ -53,6 +53,9 @@ static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreadsTc * kLaunchR
 // Dynamic shared memory budget: 227 KB per CTA minus alignment slack and the
 // barrier block.
 constexpr int kSmemBudget = 232448 - 1024 - 512;
+// Split-P scale for fp32 heads: P <= 2^8 under the stale-maximum rule, so
+// P * 2^7 stays inside fp16's range and its low part stays normal longer.
+constexpr float kSplitPScale = 128.f;
 
 template <int ELT, int DQK, int DV>
 struct TcCfg {
@@ -74,6 +77,13 @@ struct TcCfg {
     static constexpr int NSTAGE = NSTAGE_RAW > 8 ? 8 : NSTAGE_RAW;
     static_assert(NSTAGE >= 2, "ring too small");
     static constexpr int MMA_K = (ELT == 2) ? 32 : 16;   // elements per MMA k-step
+    // ELT 3: FP32 low-rank heads of 16-bit inputs. q_low, k_low (rounded to
+    // the inputs' dtype by the projection) and v are exact in fp16 once
+    // scaled by powers of two, so Q·Kᵀ and the fp32 accumulation are exact
+    // up to the accumulator; P keeps fp32 accuracy as an fp16 sum hi + lo
+    // (TMEM columns 0..63 and 64..127), each part multiplied into V.
+    static constexpr bool SPLIT = ELT == 3;
+    static_assert(!SPLIT || (DQK == 64 && DV == 128), "split operands: 64-column q/k rows, 128-column v rows");
     static constexpr int KSTEP_BYTES = MMA_K * EB;        // 32 bytes either way
     static constexpr int P_COLS = BN * EB / 4;            // TMEM columns holding P
     static constexpr uint32_t FMT = (ELT == 1) ? 1u : 0u; // bf16 = 1, f16 = 0, e4m3 = 0
@@ -341,11 +351,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             auto issue_pv = [&](int t, uint32_t stage, bool first) {
                 const uint32_t v0 = sKVa + stage * C::STAGE_BYTES;
 #pragma unroll
-                for (int ks = 0; ks < C::BN / C::MMA_K; ++ks) {
-                    const uint64_t bd = make_sdesc_sw128(v0 + ks * C::MMA_K * 128, C::BOX, 1024);
-                    const uint32_t a_t = tmem + t * 128 + ks * (C::MMA_K * C::EB / 4);
-                    issue_mma_ts<ELT>(tmem + 256 + t * DV, a_t, bd, C::IDESC_PV,
-                                      (!first || ks > 0) ? 1u : 0u);
+                for (int part = 0; part < (C::SPLIT ? 2 : 1); ++part) {
+#pragma unroll
+                    for (int ks = 0; ks < C::BN / C::MMA_K; ++ks) {
+                        const uint64_t bd = make_sdesc_sw128(v0 + ks * C::MMA_K * 128, C::BOX, 1024);
+                        const uint32_t a_t = tmem + t * 128 + part * 64 + ks * (C::MMA_K * C::EB / 4);
+                        issue_mma_ts<ELT>(tmem + 256 + t * DV, a_t, bd, C::IDESC_PV,
+                                          (!first || part > 0 || ks > 0) ? 1u : 0u);
+                    }
                 }
             };
             while (ok && take_item(bars, ic, it, abort_flag, tmo, status)) {
@@ -444,7 +457,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             const int qrow = tile_r0 + row;
             const int Nk = static_cast<int>(L.Nk);
             float sq = 1.f;
-            if constexpr (ELT == 2) sq = L.q_scale[w.bh * L.nt_q + (w.qtp * 2 + t)];
+            if constexpr (ELT >= 2) sq = L.q_scale[w.bh * L.nt_q + (w.qtp * 2 + t)];
             float m_run = -INFINITY;
             float l_run = 0.f;
             for (int j = 0; j < nt; ++j) {
@@ -473,7 +486,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     }
                 }
                 float sl2 = scale_log2;
-                if constexpr (ELT == 2) sl2 *= sq * L.k_scale[w.bh * L.nt_k + j];
+                if constexpr (ELT >= 2) sl2 *= sq * L.k_scale[w.bh * L.nt_k + j];
                 const int kv0 = j * 128;
                 const bool edge = (kv0 + 128 > Nk) || (causal && kv0 + 127 > tile_r0);
                 if (edge) {
@@ -532,8 +545,35 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 {
                     constexpr int NP = C::P_COLS / 32;  // 32-column chunks of P
                     uint32_t pr[32];
+                    if constexpr (C::SPLIT) {
+                        // P * 2^7 = hi + lo, both fp16 (hi <= 2^15); hi over
+                        // S columns 0..63, lo over 64..127, 16 columns at a time.
 #pragma unroll
-                    for (int chunk = 0; chunk < NP; ++chunk) {
+                        for (int q16 = 0; q16 < 4; ++q16) {
+                            uint32_t ph[16], pl[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const int c = q16 * 32 + i * 2;
+                                float p0, p1;
+                                f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2p, nmp), p0, p1);
+                                p0 = fast_exp2(p0);
+                                p1 = fast_exp2(p1);
+                                if (i & 1)
+                                    ls1 = f2_add(ls1, f2_pack(p0, p1));
+                                else
+                                    ls0 = f2_add(ls0, f2_pack(p0, p1));
+                                const float h0 = p0 * kSplitPScale, h1 = p1 * kSplitPScale;
+                                ph[i] = pack_f16x2(h0, h1);
+                                float r0, r1;
+                                unpack_f16x2(ph[i], r0, r1);
+                                pl[i] = pack_f16x2(h0 - r0, h1 - r1);
+                            }
+                            tmem_st16(tS + q16 * 16, ph);
+                            tmem_st16(tS + 64 + q16 * 16, pl);
+                        }
+                    }
+#pragma unroll
+                    for (int chunk = 0; chunk < (C::SPLIT ? 0 : NP); ++chunk) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             if constexpr (ELT == 2) {
@@ -599,6 +639,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             // ---- epilogue: O / l, rounded like the reference's result, stored ----
             float post = 1.f / l_run;
             if constexpr (ELT == 2) post *= L.v_scale[w.bh] * (1.f / 448.f);
+            if constexpr (ELT == 3) post *= L.v_scale[w.bh] * (1.f / kSplitPScale);
             const bool row_ok = qrow < L.Nq;
             uint8_t* orow = reinterpret_cast<uint8_t*>(L.out);
             const int64_t obase = w.b * L.os[0] + w.h * L.os[1] + static_cast<int64_t>(qrow) * L.os[2];
@@ -748,6 +789,10 @@ int launch_variant(const TcLaunch& L, cudaStream_t stream) {
 }  // namespace
 
 int launch_fmha_tc(const TcLaunch& L, cudaStream_t stream) {
+    if (L.elt == 3) {
+        if (L.dqk == 64 && L.dv == 128) return launch_variant<3, 64, 128>(L, stream);
+        return ADA_ERR_UNSUPPORTED;
+    }
     if (L.elt == 2) {
         if (L.dqk == 128 && L.dv == 128) return launch_variant<2, 128, 128>(L, stream);
         return ADA_ERR_UNSUPPORTED;

@@ -8,6 +8,10 @@
 //   prep32  FP32 low-rank heads: q_low / k_low in fp32 for the SIMT kernel.
 //   prep8   FP8 heads in E4M3 mode: per-tile amax, then tile-scaled E4M3
 //           values (Q, K: one scale per 128-row tile; V: one per head).
+//   split   FP32 low-rank heads of 16-bit inputs for the tensor cores:
+//           q_low / k_low (already rounded to the inputs' dtype) scaled by a
+//           power of two per 128-row tile, v by one per head, into fp16 --
+//           exact for 16-bit values inside fp16's range after scaling.
 #include "ada_common.cuh"
 #include "ada_internal.h"
 
@@ -380,6 +384,100 @@ int launch_prep16(const PrepLaunch& L, cudaStream_t stream) {
     return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
 
+// Power of two s with max|x| / s < 2^15: the scaled values and their fp16
+// high parts stay below fp16's largest finite value (65504).
+__device__ __forceinline__ float split_scale(float amax) {
+    if (!(amax > 0.f) || !(amax < INFINITY)) return 1.f;
+    int e;
+    frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
+    return ldexpf(1.f, e - 15 < -126 ? -126 : e - 15);
+}
+
+__device__ __forceinline__ float block_max256(float v, float* red) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float m = red[0];
+#pragma unroll
+    for (int i = 1; i < kThreads / 32; ++i) m = fmaxf(m, red[i]);
+    return m;
+}
+
+__device__ __forceinline__ bool split_head(const PrepLaunch& L, int64_t bh) {
+    int prec, low;
+    get_decision(L.dec, bh, &prec, &low);
+    return low && ((L.split_mask >> prec) & 1u);
+}
+
+// max |v| of one 128-row tile of a selected head, folded into amax_v[bh].
+__global__ void __launch_bounds__(kThreads) split_vamax_kernel(const __grid_constant__ PrepLaunch L) {
+    __shared__ float red[kThreads / 32];
+    const int64_t bh = blockIdx.y;
+    if (!split_head(L, bh)) return;
+    const int64_t b = bh / L.H, h = bh % L.H;
+    const int D = static_cast<int>(L.D);
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * 128;
+    const int64_t rows = (L.Nk - row0) < 128 ? (L.Nk - row0) : 128;
+    const int64_t base = b * L.vs[0] + h * L.vs[1];
+    float a = 0.f;
+    for (int64_t i = threadIdx.x; i < rows * D; i += kThreads) {
+        const int64_t rr = i / D;
+        const int d = static_cast<int>(i - rr * D);
+        a = fmaxf(a, fabsf(load_as_f32(L.v, base + (row0 + rr) * L.vs[2] + d * L.vs[3], L.in_dtype)));
+    }
+    a = block_max256(a, red);
+    if (threadIdx.x == 0) atomicMax(L.split_amax_v + bh, __float_as_uint(a));  // a >= 0: bits order as values
+}
+
+// One 128-row tile of q_low, k_low and v of a selected head.
+__global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__ PrepLaunch L) {
+    __shared__ float red[kThreads / 32];
+    const int64_t bh = blockIdx.y;
+    if (!split_head(L, bh)) return;
+    const int64_t tile = blockIdx.x;
+    const int r = static_cast<int>(L.r);
+    for (int which = 0; which < 2; ++which) {
+        const int64_t N = which == 0 ? L.Nq : L.Nk;
+        const int64_t nt = which == 0 ? L.nt_q : L.nt_k;
+        if (tile >= nt) continue;
+        const int64_t row0 = tile * 128;
+        const int rows = static_cast<int>((N - row0) < 128 ? (N - row0) : 128);
+        const float* src = (which == 0 ? L.ws32_q : L.ws32_k) + (bh * N + row0) * r;
+        float a = 0.f;
+        for (int i = threadIdx.x; i < rows * r; i += kThreads) a = fmaxf(a, fabsf(src[i]));
+        const float sc = split_scale(block_max256(a, red));
+        if (threadIdx.x == 0) (which == 0 ? L.split_sq : L.split_sk)[bh * nt + tile] = sc;
+        const float inv = 1.f / sc;  // a power of two: exact
+        uint16_t* dst = (which == 0 ? L.wss_q : L.wss_k) + (bh * N + row0) * 64;
+        for (int i = threadIdx.x; i < rows * 32; i += kThreads) {
+            const int rr = i >> 5, c = (i & 31) * 2;
+            const float x0 = c < r ? src[rr * r + c] * inv : 0.f;
+            const float x1 = c + 1 < r ? src[rr * r + c + 1] * inv : 0.f;
+            reinterpret_cast<uint32_t*>(dst + rr * 64)[c >> 1] = pack_f16x2(x0, x1);
+        }
+    }
+    if (tile < L.nt_k) {
+        const float sv = split_scale(__uint_as_float(L.split_amax_v[bh]));
+        if (tile == 0 && threadIdx.x == 0) L.split_sv[bh] = sv;
+        const float inv = 1.f / sv;
+        const int64_t b = bh / L.H, h = bh % L.H;
+        const int D = static_cast<int>(L.D);
+        const int64_t row0 = tile * 128;
+        const int rows = static_cast<int>((L.Nk - row0) < 128 ? (L.Nk - row0) : 128);
+        const int64_t base = b * L.vs[0] + h * L.vs[1];
+        uint16_t* dst = L.wss_v + (bh * L.Nk + row0) * 128;
+        for (int i = threadIdx.x; i < rows * 64; i += kThreads) {
+            const int rr = i >> 6, c = (i & 63) * 2;
+            const int64_t off = base + (row0 + rr) * L.vs[2];
+            const float x0 = c < D ? load_as_f32(L.v, off + c * L.vs[3], L.in_dtype) * inv : 0.f;
+            const float x1 = c + 1 < D ? load_as_f32(L.v, off + (c + 1) * L.vs[3], L.in_dtype) * inv : 0.f;
+            reinterpret_cast<uint32_t*>(dst + rr * 128)[c >> 1] = pack_f16x2(x0, x1);
+        }
+    }
+}
+
 int launch_cast16(const PrepLaunch& L, int skip_low_rank_qk, cudaStream_t stream) {
     const int64_t nt = ((L.Nq > L.Nk ? L.Nq : L.Nk) + kRows - 1) / kRows;
     if (nt == 0 || L.B * L.H == 0) return ADA_OK;
@@ -402,6 +500,18 @@ int launch_prep32(const PrepLaunch& L, cudaStream_t stream) {
     const size_t smem = proj_smem(L, true);
     if (set_smem(prep32_kernel, smem) != ADA_OK) return ADA_ERR_LAUNCH;
     prep32_kernel<<<dim3(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H)), kThreads, smem, stream>>>(L);
+    return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+}
+
+int launch_split(const PrepLaunch& L, cudaStream_t stream) {
+    const int64_t nt = L.nt_q > L.nt_k ? L.nt_q : L.nt_k;
+    if (nt == 0 || L.B * L.H == 0) return ADA_OK;
+    if (L.nt_k > 0) {
+        split_vamax_kernel<<<dim3(static_cast<unsigned>(L.nt_k), static_cast<unsigned>(L.B * L.H)), kThreads, 0,
+                             stream>>>(L);
+        if (cudaGetLastError() != cudaSuccess) return ADA_ERR_LAUNCH;
+    }
+    split_kernel<<<dim3(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H)), kThreads, 0, stream>>>(L);
     return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
 

@@ -99,6 +99,10 @@ LOW_CASES = [
     (torch.bfloat16, O.BF16, 64, 100, 128),    # r_pad 128 > D: SIMT projection
     (torch.bfloat16, O.FP32, 128, 100, 150),   # pipelined CUDA-core path, bf16 V
     (torch.float32, O.FP32, 128, 30, 100),     # rank not a multiple of 4: unpipelined path
+    # FP32 heads of 16-bit inputs with r <= 64: tensor cores, P as fp16 hi + lo
+    (torch.bfloat16, O.FP32, 64, 32, 300),     # V padded from 64 to 128 columns
+    (torch.float16, O.FP32, 128, 17, 129),
+    (torch.bfloat16, O.FP32, 128, 64, 1),
 ]
 
 
@@ -174,3 +178,68 @@ def test_fully_masked_row_is_nan_like_reference(cuda_device):
         assert torch.isnan(ref[0, 0, 3]).all()
         assert torch.isnan(out[0, 0, 3]).all()
         assert not torch.isnan(out[0, 0, :3]).any()
+
+
+def _low_rank_truth(q, k, v, w, scale, causal):
+    """The reference's FP32 low-rank branch evaluated in float64 after its
+    16-bit projection, rounded once to the inputs' dtype."""
+    ql = torch.nn.functional.linear(q, w).double()
+    kl = torch.nn.functional.linear(k, w).double()
+    s = ql @ kl.transpose(-1, -2) * scale
+    if causal:
+        hide = torch.triu(torch.ones(s.shape[-2], s.shape[-1], dtype=torch.bool), 1)
+        s = s.masked_fill(hide, float("-inf"))
+    return (torch.softmax(s, -1) @ v.double()).to(q.dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("causal", [False, True])
+def test_fp32_low_rank_tensor_core_bits(dtype, causal, cuda_device):
+    """FP32 low-rank heads of 16-bit inputs run on the tensor cores with P as
+    an fp16 sum hi + lo. Rounded to the output dtype, the result must agree
+    with the float64 evaluation of the same branch nearly as often as the
+    reference's own fp32 arithmetic does, on peaked scores (|s| up to ~400).
+
+    The projection is the identity (D = r = 64), so q_low and k_low are the
+    inputs on both sides: with a general rank_proj_down, a one-unit rounding
+    difference of a 16-bit q_low element between two summation orders moves
+    such scores by ~0.1 and dominates every other difference.
+
+    Measured on these inputs (bf16 / fp16 outputs): the kernel agrees with
+    float64 on 99.97 % / 99.83 % of the elements, the reference's fp32 path
+    on 99.96-99.98 % / 99.60-99.69 %; P rounded to fp16 alone (no low part)
+    would agree on 99.70 % / 98.59 %, outside the slack below."""
+    q, k, v = _inputs(2, 2, 384, 384, 64, dtype, seed=21, scale=10.0)
+    w = torch.eye(64).to(dtype)
+    out, scale = _run(q, k, v, O.FP32, True, causal, cuda_device, w=w)
+    ref = O.low_rank_attention(q, k, v, w, O.FP32, scale, causal)
+    truth = _low_rank_truth(q, k, v, w, scale, causal)
+    ours = (out == truth).float().mean().item()
+    theirs = (ref == truth).float().mean().item()
+    print(f"FP32-split {dtype} causal={causal}: agrees with float64 on {ours:.5f}, reference fp32 {theirs:.5f}, "
+          f"with reference {(out == ref).float().mean().item():.5f}")
+    assert ours >= theirs - SPLIT_SLACK[dtype], f"{ours:.5f} vs reference {theirs:.5f}"
+    for h in range(2):
+        check_head(out[:, h:h + 1], q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], O.FP32, True,
+                   scale, causal, w_down=w, label=f"h{h}")
+
+
+SPLIT_SLACK = {torch.bfloat16: 0.0005, torch.float16: 0.002}
+
+
+def test_fp32_low_rank_tensor_core_masks(cuda_device):
+    q, k, v = _inputs(2, 2, 96, 160, 128, torch.bfloat16, seed=22, scale=4.0)
+    w = _w_down(128, 64, torch.bfloat16)
+    g = torch.Generator().manual_seed(23)
+    keep = torch.rand(2, 1, 96, 160, generator=g) > 0.3
+    keep[..., 0] = True
+    keep[0, 0, 5] = False  # a fully masked row: NaN, as in the reference
+    add = torch.randn(2, 1, 96, 160, generator=g)
+    for mask in (keep, add):
+        out, scale = _run(q, k, v, O.FP32, True, False, cuda_device, mask=mask, w=w)
+        ref = O.low_rank_attention(q, k, v, w, O.FP32, scale, False, mask)
+        assert torch.equal(torch.isnan(out), torch.isnan(ref))
+        ok = ~torch.isnan(ref)
+        m = max(1.0, ref[ok].abs().max().item())
+        err = (out[ok].float() - ref[ok].float()).abs().max().item()
+        assert err <= 1e-5 * m + 2.0 ** -8 * m, f"mask {mask.dtype}: err {err:.3e}"
