@@ -129,10 +129,14 @@ struct PrepLaunch {
     float* scale_v; // [B,H]
     int64_t nt_q, nt_k;
     int low_src16;  // 1: low-rank q_low/k_low are already in the 16-bit region (input dtype)
-    // FP32 low-rank heads of 16-bit inputs on the tensor cores: q_low/k_low
-    // (fp32 region, values of the inputs' dtype) and v scaled by powers of
-    // two into fp16: q, k [B*H][N][64], v [B*H][N][128].
+    // FP32 heads of 16-bit inputs on the tensor cores: q, k (dense heads) or
+    // q_low, k_low (low-rank heads with r <= 64, from the fp32 region; values
+    // of the inputs' dtype) and v scaled by powers of two into fp16:
+    // q, k [B*H][N][split_ld] (64 columns for low rank, dqk_dense for dense
+    // heads), v [B*H][N][128].
     uint32_t split_mask;      // precision codes served this way (FP32) or 0
+    int split_low, split_dense;  // which FP32 heads (low rank / dense) are served
+    int64_t split_ld;
     uint16_t* wss_q;
     uint16_t* wss_k;
     uint16_t* wss_v;

@@ -220,7 +220,9 @@ struct Plan {
     int dqk_dense, dqk_low, dv_pad;
     int64_t ld16_qk, ld16_v;
     bool need16, need32, need8;
-    bool split;          // FP32 low-rank heads on the tensor cores as split fp16 operands
+    bool split;          // some FP32 heads run on the tensor cores (scaled fp16 operands, split P)
+    bool split_low, split_dense;
+    int64_t split_ld;    // row width of the split q/k region
     bool proj_tc_shape;  // low-rank projection can run on the tensor cores
     int64_t nt_q, nt_k;
     size_t off16q, off16k, off16v, off32q, off32k, off8q, off8k, off8v;
@@ -307,10 +309,17 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
     }
     P->need32 = ((P->possible & P->fp32_mask) != 0) && P->low_possible;
     P->need8 = (P->possible & P->fp8_mask) != 0;
-    // FP32 low-rank heads of 16-bit inputs with r <= 64: fp32-accurate on the
-    // tensor cores (split fp16 operands); dense FP32 heads, wider ranks and
-    // fp32 inputs stay on the CUDA cores.
-    P->split = P->need32 && P->r <= 64 && (P->in_dtype == ADA_F16 || P->in_dtype == ADA_BF16);
+    // FP32 heads of 16-bit inputs (dense, or low rank with r <= 64) run
+    // fp32-accurate on the tensor cores (scaled fp16 operands, split P);
+    // wider ranks and fp32 inputs stay on the CUDA cores.
+    {
+        const bool in16 = P->in_dtype == ADA_F16 || P->in_dtype == ADA_BF16;
+        const bool fp32 = (P->possible & P->fp32_mask) != 0;
+        P->split_low = in16 && P->need32 && P->r <= 64;
+        P->split_dense = in16 && fp32 && P->dense_possible;
+        P->split = P->split_low || P->split_dense;
+        P->split_ld = P->split_dense ? P->dqk_dense : 64;
+    }
     // E4M3 low-rank heads take their projection from the tensor-core kernel,
     // which writes q_low/k_low into the 16-bit region.
     P->proj_tc_shape = P->low_possible && P->direct_ok &&
@@ -336,9 +345,9 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
     }
     if (P->split) {
         P->offs_q = off;
-        off = align256(off + static_cast<size_t>(BH * P->Nq * 64) * 2);
+        off = align256(off + static_cast<size_t>(BH * P->Nq * P->split_ld) * 2);
         P->offs_k = off;
-        off = align256(off + static_cast<size_t>(BH * P->Nk * 64) * 2);
+        off = align256(off + static_cast<size_t>(BH * P->Nk * P->split_ld) * 2);
         P->offs_v = off;
         off = align256(off + static_cast<size_t>(BH * P->Nk * 128) * 2);
         P->offs_sq = off;
@@ -669,6 +678,9 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
 
     if (P.split) {
         pl.split_mask = P.fp32_mask;
+        pl.split_low = P.split_low ? 1 : 0;
+        pl.split_dense = P.split_dense ? 1 : 0;
+        pl.split_ld = P.split_ld;
         pl.wss_q = reinterpret_cast<uint16_t*>(ws + P.offs_q);
         pl.wss_k = reinterpret_cast<uint16_t*>(ws + P.offs_k);
         pl.wss_v = reinterpret_cast<uint16_t*>(ws + P.offs_v);
@@ -769,28 +781,37 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
             if ((rc = launch_fmha_tc(L, s))) return fail(rc, "E4M3 attention launch failed");
         }
     }
-    if (P.split) {
+    for (int low = 0; low < 2; ++low) {
+        if (!(low ? P.split_low : P.split_dense)) continue;
         TcLaunch L;
         base_tc(L);
         L.elt = 3;
         L.round_dtype = ADA_F32;
-        L.sel = HeadSelect{decisions, P.fp32_mask, 1};
-        L.dqk = 64;
+        L.sel = HeadSelect{decisions, P.fp32_mask, low};
+        L.dqk = low ? 64 : P.dqk_dense;
         L.dv = 128;
         L.q_scale = reinterpret_cast<float*>(ws + P.offs_sq);
         L.k_scale = reinterpret_cast<float*>(ws + P.offs_sk);
         L.v_scale = reinterpret_cast<float*>(ws + P.offs_sv);
         const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-        if ((rc = make_map(&L.tq, ws + P.offs_q, dt, 2, 64, P.Nq, P.H, P.B, 64, P.Nq * 64, P.H * P.Nq * 64)) ||
-            (rc = make_map(&L.tk, ws + P.offs_k, dt, 2, 64, P.Nk, P.H, P.B, 64, P.Nk * 64, P.H * P.Nk * 64)) ||
+        const int64_t l = P.split_ld;
+        if ((rc = make_map(&L.tq, ws + P.offs_q, dt, 2, L.dqk, P.Nq, P.H, P.B, l, P.Nq * l, P.H * P.Nq * l)) ||
+            (rc = make_map(&L.tk, ws + P.offs_k, dt, 2, L.dqk, P.Nk, P.H, P.B, l, P.Nk * l, P.H * P.Nk * l)) ||
             (rc = make_map(&L.tv, ws + P.offs_v, dt, 2, 128, P.Nk, P.H, P.B, 128, P.Nk * 128, P.H * P.Nk * 128)))
             return rc;
-        if ((rc = launch_fmha_tc(L, s))) return fail(rc, "split fp32 attention launch failed");
+        if (L.dqk == 128 && P.D == 128 && (out->dtype == ADA_F16 || out->dtype == ADA_BF16) && out->stride[3] == 1 &&
+            out_vec_bytes(out) >= 16) {
+            if ((rc = make_map(&L.to, out->data, tma_dtype(out->dtype), 2, P.D, P.Nq, P.H, P.B, out->stride[2],
+                               out->stride[1], out->stride[0])))
+                return rc;
+            L.tma_out = 1;
+        }
+        if ((rc = launch_fmha_tc(L, s))) return fail(rc, "fp32 tensor-core attention launch failed");
     }
     // ---- fp32 heads on the CUDA cores ---------------------------------------
     if (P.possible & P.fp32_mask) {
         for (int low = 0; low < 2; ++low) {
-            if (low ? (!P.low_possible || P.split) : !P.dense_possible) continue;
+            if (low ? (!P.low_possible || P.split_low) : (!P.dense_possible || P.split_dense)) continue;
             SimtLaunch L{};
             L.B = P.B;
             L.H = P.H;

@@ -77,13 +77,13 @@ struct TcCfg {
     static constexpr int NSTAGE = NSTAGE_RAW > 8 ? 8 : NSTAGE_RAW;
     static_assert(NSTAGE >= 2, "ring too small");
     static constexpr int MMA_K = (ELT == 2) ? 32 : 16;   // elements per MMA k-step
-    // ELT 3: FP32 low-rank heads of 16-bit inputs. q_low, k_low (rounded to
+    // ELT 3: FP32 heads of 16-bit inputs. q, k (or q_low, k_low, rounded to
     // the inputs' dtype by the projection) and v are exact in fp16 once
     // scaled by powers of two, so Q·Kᵀ and the fp32 accumulation are exact
     // up to the accumulator; P keeps fp32 accuracy as an fp16 sum hi + lo
     // (TMEM columns 0..63 and 64..127), each part multiplied into V.
     static constexpr bool SPLIT = ELT == 3;
-    static_assert(!SPLIT || (DQK == 64 && DV == 128), "split operands: 64-column q/k rows, 128-column v rows");
+    static_assert(!SPLIT || DV == 128, "split operands: 128-column v rows");
     static constexpr int KSTEP_BYTES = MMA_K * EB;        // 32 bytes either way
     static constexpr int P_COLS = BN * EB / 4;            // TMEM columns holding P
     static constexpr uint32_t FMT = (ELT == 1) ? 1u : 0u; // bf16 = 1, f16 = 0, e4m3 = 0
@@ -790,6 +790,7 @@ int launch_variant(const TcLaunch& L, cudaStream_t stream) {
 
 int launch_fmha_tc(const TcLaunch& L, cudaStream_t stream) {
     if (L.elt == 3) {
+        if (L.dqk == 128 && L.dv == 128) return launch_variant<3, 128, 128>(L, stream);
         if (L.dqk == 64 && L.dv == 128) return launch_variant<3, 64, 128>(L, stream);
         return ADA_ERR_UNSUPPORTED;
     }

@@ -405,17 +405,20 @@ __device__ __forceinline__ float block_max256(float v, float* red) {
     return m;
 }
 
-__device__ __forceinline__ bool split_head(const PrepLaunch& L, int64_t bh) {
+// 0: not served; 1: low-rank head; 2: dense head.
+__device__ __forceinline__ int split_head(const PrepLaunch& L, int64_t bh) {
     int prec, low;
     get_decision(L.dec, bh, &prec, &low);
-    return low && ((L.split_mask >> prec) & 1u);
+    if (!((L.split_mask >> prec) & 1u)) return 0;
+    if (low) return L.split_low ? 1 : 0;
+    return L.split_dense ? 2 : 0;
 }
 
 // max |v| of one 128-row tile of a selected head, folded into amax_v[bh].
 __global__ void __launch_bounds__(kThreads) split_vamax_kernel(const __grid_constant__ PrepLaunch L) {
     __shared__ float red[kThreads / 32];
     const int64_t bh = blockIdx.y;
-    if (!split_head(L, bh)) return;
+    if (split_head(L, bh) == 0) return;
     const int64_t b = bh / L.H, h = bh % L.H;
     const int D = static_cast<int>(L.D);
     const int64_t row0 = static_cast<int64_t>(blockIdx.x) * 128;
@@ -435,34 +438,48 @@ __global__ void __launch_bounds__(kThreads) split_vamax_kernel(const __grid_cons
 __global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__ PrepLaunch L) {
     __shared__ float red[kThreads / 32];
     const int64_t bh = blockIdx.y;
-    if (!split_head(L, bh)) return;
+    const int kind = split_head(L, bh);
+    if (kind == 0) return;
+    const int64_t b = bh / L.H, h = bh % L.H;
     const int64_t tile = blockIdx.x;
-    const int r = static_cast<int>(L.r);
+    // low rank: fp32 q_low/k_low [B*H][N][r] -> 64 columns;
+    // dense: the 16-bit inputs (any strides) -> dqk_dense columns
+    const int width = kind == 1 ? static_cast<int>(L.r) : static_cast<int>(L.D);
+    const int wout = kind == 1 ? 64 : L.dqk_dense;
     for (int which = 0; which < 2; ++which) {
         const int64_t N = which == 0 ? L.Nq : L.Nk;
         const int64_t nt = which == 0 ? L.nt_q : L.nt_k;
         if (tile >= nt) continue;
         const int64_t row0 = tile * 128;
         const int rows = static_cast<int>((N - row0) < 128 ? (N - row0) : 128);
-        const float* src = (which == 0 ? L.ws32_q : L.ws32_k) + (bh * N + row0) * r;
+        const float* src32 = (which == 0 ? L.ws32_q : L.ws32_k) + (bh * N + row0) * width;
+        const void* src16 = which == 0 ? L.q : L.k;
+        const int64_t* st = which == 0 ? L.qs : L.ks;
+        const int64_t base16 = b * st[0] + h * st[1] + row0 * st[2];
+        auto at = [&](int rr, int c) {
+            return kind == 1 ? src32[rr * width + c] : load_as_f32(src16, base16 + rr * st[2] + c * st[3], L.in_dtype);
+        };
         float a = 0.f;
-        for (int i = threadIdx.x; i < rows * r; i += kThreads) a = fmaxf(a, fabsf(src[i]));
+        for (int i = threadIdx.x; i < rows * width; i += kThreads) {
+            const int rr = i / width, c = i - rr * width;
+            a = fmaxf(a, fabsf(at(rr, c)));
+        }
         const float sc = split_scale(block_max256(a, red));
         if (threadIdx.x == 0) (which == 0 ? L.split_sq : L.split_sk)[bh * nt + tile] = sc;
         const float inv = 1.f / sc;  // a power of two: exact
-        uint16_t* dst = (which == 0 ? L.wss_q : L.wss_k) + (bh * N + row0) * 64;
-        for (int i = threadIdx.x; i < rows * 32; i += kThreads) {
-            const int rr = i >> 5, c = (i & 31) * 2;
-            const float x0 = c < r ? src[rr * r + c] * inv : 0.f;
-            const float x1 = c + 1 < r ? src[rr * r + c + 1] * inv : 0.f;
-            reinterpret_cast<uint32_t*>(dst + rr * 64)[c >> 1] = pack_f16x2(x0, x1);
+        uint16_t* dst = (which == 0 ? L.wss_q : L.wss_k) + (bh * N + row0) * L.split_ld;
+        const int half = wout / 2;
+        for (int i = threadIdx.x; i < rows * half; i += kThreads) {
+            const int rr = i / half, c = (i - rr * half) * 2;
+            const float x0 = c < width ? at(rr, c) * inv : 0.f;
+            const float x1 = c + 1 < width ? at(rr, c + 1) * inv : 0.f;
+            reinterpret_cast<uint32_t*>(dst + rr * L.split_ld)[c >> 1] = pack_f16x2(x0, x1);
         }
     }
     if (tile < L.nt_k) {
         const float sv = split_scale(__uint_as_float(L.split_amax_v[bh]));
         if (tile == 0 && threadIdx.x == 0) L.split_sv[bh] = sv;
         const float inv = 1.f / sv;
-        const int64_t b = bh / L.H, h = bh % L.H;
         const int D = static_cast<int>(L.D);
         const int64_t row0 = tile * 128;
         const int rows = static_cast<int>((L.Nk - row0) < 128 ? (L.Nk - row0) : 128);

@@ -70,6 +70,10 @@ DENSE_CASES = [
     (torch.bfloat16, O.BF16, 32, 150, 150),    # head dim padded to 64
     (torch.float32, O.FP32, 128, 100, 300),    # pipelined CUDA-core path, fp32 K and V
     (torch.float32, O.FP32, 72, 90, 90),       # pipelined, zero-filled columns 72..127
+    # FP32 heads of 16-bit inputs: tensor cores (scaled fp16 operands, P as hi + lo)
+    (torch.float16, O.FP32, 64, 200, 77),
+    (torch.bfloat16, O.FP32, 96, 100, 100),    # head dim padded to 128
+    (torch.bfloat16, O.FP32, 128, 1, 1),
 ]
 
 
@@ -137,7 +141,7 @@ def test_fp8_reference_mode_is_fp16(cuda_device):
 
 
 @pytest.mark.parametrize("prec,dtype", [(O.BF16, torch.bfloat16), (O.FP16, torch.float32),
-                                        (O.FP32, torch.float32)])
+                                        (O.FP32, torch.float32), (O.FP32, torch.bfloat16)])
 def test_masks(prec, dtype, cuda_device):
     q, k, v = _inputs(2, 2, 96, 160, 64, dtype, seed=7)
     g = torch.Generator().manual_seed(8)
@@ -194,14 +198,15 @@ def _low_rank_truth(q, k, v, w, scale, causal):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("causal", [False, True])
-def test_fp32_low_rank_tensor_core_bits(dtype, causal, cuda_device):
-    """FP32 low-rank heads of 16-bit inputs run on the tensor cores with P as
-    an fp16 sum hi + lo. Rounded to the output dtype, the result must agree
+@pytest.mark.parametrize("low", [True, False])
+def test_fp32_tensor_core_bits(low, dtype, causal, cuda_device):
+    """FP32 heads of 16-bit inputs (dense, and low rank with r <= 64) run on
+    the tensor cores with P as an fp16 sum hi + lo. Rounded to the output dtype, the result must agree
     with the float64 evaluation of the same branch nearly as often as the
     reference's own fp32 arithmetic does, on peaked scores (|s| up to ~400).
 
-    The projection is the identity (D = r = 64), so q_low and k_low are the
-    inputs on both sides: with a general rank_proj_down, a one-unit rounding
+    The low-rank projection is the identity (D = r = 64), so q_low and k_low
+    are the inputs on both sides: with a general rank_proj_down, a one-unit rounding
     difference of a 16-bit q_low element between two summation orders moves
     such scores by ~0.1 and dominates every other difference.
 
@@ -211,17 +216,20 @@ def test_fp32_low_rank_tensor_core_bits(dtype, causal, cuda_device):
     would agree on 99.70 % / 98.59 %, outside the slack below."""
     q, k, v = _inputs(2, 2, 384, 384, 64, dtype, seed=21, scale=10.0)
     w = torch.eye(64).to(dtype)
-    out, scale = _run(q, k, v, O.FP32, True, causal, cuda_device, w=w)
-    ref = O.low_rank_attention(q, k, v, w, O.FP32, scale, causal)
-    truth = _low_rank_truth(q, k, v, w, scale, causal)
+    out, scale = _run(q, k, v, O.FP32, low, causal, cuda_device, w=w if low else None)
+    if low:
+        ref = O.low_rank_attention(q, k, v, w, O.FP32, scale, causal)
+    else:
+        ref = O.dense_attention(q, k, v, O.FP32, scale, causal)
+    truth = _low_rank_truth(q, k, v, w, scale, causal)  # identity projection: also the dense truth
     ours = (out == truth).float().mean().item()
     theirs = (ref == truth).float().mean().item()
-    print(f"FP32-split {dtype} causal={causal}: agrees with float64 on {ours:.5f}, reference fp32 {theirs:.5f}, "
+    print(f"FP32-split low={low} {dtype} causal={causal}: agrees with float64 on {ours:.5f}, reference fp32 {theirs:.5f}, "
           f"with reference {(out == ref).float().mean().item():.5f}")
     assert ours >= theirs - SPLIT_SLACK[dtype], f"{ours:.5f} vs reference {theirs:.5f}"
     for h in range(2):
-        check_head(out[:, h:h + 1], q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], O.FP32, True,
-                   scale, causal, w_down=w, label=f"h{h}")
+        check_head(out[:, h:h + 1], q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], O.FP32, low,
+                   scale, causal, w_down=w if low else None, label=f"h{h}")
 
 
 SPLIT_SLACK = {torch.bfloat16: 0.0005, torch.float16: 0.002}
