@@ -414,28 +414,69 @@ __device__ __forceinline__ int split_head(const PrepLaunch& L, int64_t bh) {
     return L.split_dense ? 2 : 0;
 }
 
+// Eight consecutive values x[row, c0 .. c0+7] as fp32, zero from column
+// `width` on. `vec`: unit column stride and 16-byte aligned rows.
+__device__ __forceinline__ void load8(const void* x, int dt, int64_t row_base, int64_t col_stride, int c0,
+                                      int width, bool vec, float (&v)[8]) {
+    if (vec && c0 + 8 <= width) {
+        const int64_t e = row_base + c0;
+        if (dt == ADA_F32) {
+            const float4 a = reinterpret_cast<const float4*>(x)[e / 4];
+            const float4 c = reinterpret_cast<const float4*>(x)[e / 4 + 1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+        } else {
+            const uint4 a = reinterpret_cast<const uint4*>(x)[e / 8];
+            const uint32_t w4[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (dt == ADA_BF16) {
+                    v[2 * k] = __uint_as_float(w4[k] << 16);
+                    v[2 * k + 1] = __uint_as_float(w4[k] & 0xffff0000u);
+                } else {
+                    unpack_f16x2(w4[k], v[2 * k], v[2 * k + 1]);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            v[k] = (c0 + k < width) ? load_as_f32(x, row_base + (c0 + k) * col_stride, dt) : 0.f;
+    }
+}
+
 // max |v| of one 128-row tile of a selected head, folded into amax_v[bh].
-__global__ void __launch_bounds__(kThreads) split_vamax_kernel(const __grid_constant__ PrepLaunch L) {
+__global__ void __launch_bounds__(kThreads) split_vamax_kernel(const __grid_constant__ PrepLaunch L, int vec_v) {
     __shared__ float red[kThreads / 32];
     const int64_t bh = blockIdx.y;
     if (split_head(L, bh) == 0) return;
     const int64_t b = bh / L.H, h = bh % L.H;
     const int D = static_cast<int>(L.D);
+    const int groups = (D + 7) / 8;
     const int64_t row0 = static_cast<int64_t>(blockIdx.x) * 128;
-    const int64_t rows = (L.Nk - row0) < 128 ? (L.Nk - row0) : 128;
+    const int rows = static_cast<int>((L.Nk - row0) < 128 ? (L.Nk - row0) : 128);
     const int64_t base = b * L.vs[0] + h * L.vs[1];
     float a = 0.f;
-    for (int64_t i = threadIdx.x; i < rows * D; i += kThreads) {
-        const int64_t rr = i / D;
-        const int d = static_cast<int>(i - rr * D);
-        a = fmaxf(a, fabsf(load_as_f32(L.v, base + (row0 + rr) * L.vs[2] + d * L.vs[3], L.in_dtype)));
+    for (int i = threadIdx.x; i < rows * groups; i += kThreads) {
+        const int rr = i / groups, g = i - rr * groups;
+        float v[8];
+        load8(L.v, L.in_dtype, base + (row0 + rr) * L.vs[2], L.vs[3], g * 8, D, vec_v != 0, v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a = fmaxf(a, fabsf(v[k]));
     }
     a = block_max256(a, red);
     if (threadIdx.x == 0) atomicMax(L.split_amax_v + bh, __float_as_uint(a));  // a >= 0: bits order as values
 }
 
-// One 128-row tile of q_low, k_low and v of a selected head.
-__global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__ PrepLaunch L) {
+__device__ __forceinline__ uint4 pack8_f16(const float (&v)[8], float inv) {
+    return make_uint4(pack_f16x2(v[0] * inv, v[1] * inv), pack_f16x2(v[2] * inv, v[3] * inv),
+                      pack_f16x2(v[4] * inv, v[5] * inv), pack_f16x2(v[6] * inv, v[7] * inv));
+}
+
+// One 128-row tile of q (or q_low), k (or k_low) and v of a selected head.
+// vec_*: the source's rows allow 16-byte loads.
+__global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__ PrepLaunch L, int vec_q, int vec_k,
+                                                         int vec_v) {
     __shared__ float red[kThreads / 32];
     const int64_t bh = blockIdx.y;
     const int kind = split_head(L, bh);
@@ -446,34 +487,57 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__
     // dense: the 16-bit inputs (any strides) -> dqk_dense columns
     const int width = kind == 1 ? static_cast<int>(L.r) : static_cast<int>(L.D);
     const int wout = kind == 1 ? 64 : L.dqk_dense;
+    const int groups = wout / 8;
     for (int which = 0; which < 2; ++which) {
         const int64_t N = which == 0 ? L.Nq : L.Nk;
         const int64_t nt = which == 0 ? L.nt_q : L.nt_k;
         if (tile >= nt) continue;
         const int64_t row0 = tile * 128;
         const int rows = static_cast<int>((N - row0) < 128 ? (N - row0) : 128);
-        const float* src32 = (which == 0 ? L.ws32_q : L.ws32_k) + (bh * N + row0) * width;
-        const void* src16 = which == 0 ? L.q : L.k;
-        const int64_t* st = which == 0 ? L.qs : L.ks;
-        const int64_t base16 = b * st[0] + h * st[1] + row0 * st[2];
-        auto at = [&](int rr, int c) {
-            return kind == 1 ? src32[rr * width + c] : load_as_f32(src16, base16 + rr * st[2] + c * st[3], L.in_dtype);
-        };
+        const void* src;
+        int dt;
+        int64_t base, rs, cs;
+        bool vec;
+        if (kind == 1) {
+            src = which == 0 ? L.ws32_q : L.ws32_k;
+            dt = ADA_F32;
+            base = (bh * N + row0) * width;
+            rs = width;
+            cs = 1;
+            vec = (width % 4) == 0;
+        } else {
+            const int64_t* st = which == 0 ? L.qs : L.ks;
+            src = which == 0 ? L.q : L.k;
+            dt = L.in_dtype;
+            base = b * st[0] + h * st[1] + row0 * st[2];
+            rs = st[2];
+            cs = st[3];
+            vec = (which == 0 ? vec_q : vec_k) != 0;
+        }
+        // at most 128 rows x 16 groups = 8 groups per thread, held in registers
+        float x[8][8];
         float a = 0.f;
-        for (int i = threadIdx.x; i < rows * width; i += kThreads) {
-            const int rr = i / width, c = i - rr * width;
-            a = fmaxf(a, fabsf(at(rr, c)));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * kThreads;
+            if (i < rows * groups) {
+                const int rr = i / groups, g = i - rr * groups;
+                load8(src, dt, base + rr * rs, cs, g * 8, width, vec, x[u]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) a = fmaxf(a, fabsf(x[u][k]));
+            }
         }
         const float sc = split_scale(block_max256(a, red));
         if (threadIdx.x == 0) (which == 0 ? L.split_sq : L.split_sk)[bh * nt + tile] = sc;
         const float inv = 1.f / sc;  // a power of two: exact
         uint16_t* dst = (which == 0 ? L.wss_q : L.wss_k) + (bh * N + row0) * L.split_ld;
-        const int half = wout / 2;
-        for (int i = threadIdx.x; i < rows * half; i += kThreads) {
-            const int rr = i / half, c = (i - rr * half) * 2;
-            const float x0 = c < width ? at(rr, c) * inv : 0.f;
-            const float x1 = c + 1 < width ? at(rr, c + 1) * inv : 0.f;
-            reinterpret_cast<uint32_t*>(dst + rr * L.split_ld)[c >> 1] = pack_f16x2(x0, x1);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * kThreads;
+            if (i < rows * groups) {
+                const int rr = i / groups, g = i - rr * groups;
+                reinterpret_cast<uint4*>(dst + rr * L.split_ld)[g] = pack8_f16(x[u], inv);
+            }
         }
     }
     if (tile < L.nt_k) {
@@ -485,12 +549,11 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__
         const int rows = static_cast<int>((L.Nk - row0) < 128 ? (L.Nk - row0) : 128);
         const int64_t base = b * L.vs[0] + h * L.vs[1];
         uint16_t* dst = L.wss_v + (bh * L.Nk + row0) * 128;
-        for (int i = threadIdx.x; i < rows * 64; i += kThreads) {
-            const int rr = i >> 6, c = (i & 63) * 2;
-            const int64_t off = base + (row0 + rr) * L.vs[2];
-            const float x0 = c < D ? load_as_f32(L.v, off + c * L.vs[3], L.in_dtype) * inv : 0.f;
-            const float x1 = c + 1 < D ? load_as_f32(L.v, off + (c + 1) * L.vs[3], L.in_dtype) * inv : 0.f;
-            reinterpret_cast<uint32_t*>(dst + rr * 128)[c >> 1] = pack_f16x2(x0, x1);
+        for (int i = threadIdx.x; i < rows * 16; i += kThreads) {
+            const int rr = i >> 4, g = i & 15;
+            float v[8];
+            load8(L.v, L.in_dtype, base + (row0 + rr) * L.vs[2], L.vs[3], g * 8, D, vec_v != 0, v);
+            reinterpret_cast<uint4*>(dst + rr * 128)[g] = pack8_f16(v, inv);
         }
     }
 }
@@ -523,12 +586,21 @@ int launch_prep32(const PrepLaunch& L, cudaStream_t stream) {
 int launch_split(const PrepLaunch& L, cudaStream_t stream) {
     const int64_t nt = L.nt_q > L.nt_k ? L.nt_q : L.nt_k;
     if (nt == 0 || L.B * L.H == 0) return ADA_OK;
+    const int eb = L.in_dtype == ADA_F32 ? 4 : 2;
+    auto vec_ok = [&](const void* p, const int64_t* st) {
+        if (st[3] != 1 || (reinterpret_cast<uintptr_t>(p) & 15u) != 0) return 0;
+        for (int i = 0; i < 3; ++i)
+            if (((st[i] * eb) % 16) != 0) return 0;
+        return 1;
+    };
+    const int vv = vec_ok(L.v, L.vs);
     if (L.nt_k > 0) {
         split_vamax_kernel<<<dim3(static_cast<unsigned>(L.nt_k), static_cast<unsigned>(L.B * L.H)), kThreads, 0,
-                             stream>>>(L);
+                             stream>>>(L, vv);
         if (cudaGetLastError() != cudaSuccess) return ADA_ERR_LAUNCH;
     }
-    split_kernel<<<dim3(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H)), kThreads, 0, stream>>>(L);
+    split_kernel<<<dim3(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H)), kThreads, 0, stream>>>(
+        L, vec_ok(L.q, L.qs), vec_ok(L.k, L.ks), vv);
     return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
 }
 
