@@ -558,6 +558,115 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__
     }
 }
 
+// E4M3 heads whose q, k need no projection here (dense heads, or low-rank
+// heads whose q_low / k_low the tensor-core projection already wrote to the
+// 16-bit region): pass 0 takes each V tile's amax; pass 1 quantises q and k
+// with one scale per 128-row tile (the tile held in registers between its
+// amax and its stores) and v with the head's scale. Same arithmetic as
+// prep8: scale = amax / 448, e4m3(x / scale) saturating.
+__global__ void __launch_bounds__(kThreads) quant8_kernel(const __grid_constant__ PrepLaunch L, int pass, int vec_q,
+                                                          int vec_k, int vec_v) {
+    __shared__ float red[kThreads / 32];
+    const int64_t bh = blockIdx.y;
+    int prec, low;
+    get_decision(L.dec, bh, &prec, &low);
+    if (!((L.fp8_mask >> prec) & 1u)) return;
+    const int64_t b = bh / L.H, h = bh % L.H;
+    const int D = static_cast<int>(L.D);
+    const int64_t tile = blockIdx.x;
+    if (pass == 0) {
+        if (tile >= L.nt_k) return;
+        const int64_t row0 = tile * 128;
+        const int rows = static_cast<int>((L.Nk - row0) < 128 ? (L.Nk - row0) : 128);
+        const int groups = (D + 7) / 8;
+        const int64_t base = b * L.vs[0] + h * L.vs[1];
+        float a = 0.f;
+        for (int i = threadIdx.x; i < rows * groups; i += kThreads) {
+            const int rr = i / groups, g = i - rr * groups;
+            float v[8];
+            load8(L.v, L.in_dtype, base + (row0 + rr) * L.vs[2], L.vs[3], g * 8, D, vec_v != 0, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) a = fmaxf(a, fabsf(v[k]));
+        }
+        a = block_max256(a, red);
+        if (threadIdx.x == 0) L.amax_v[bh * L.nt_k + tile] = a;
+        return;
+    }
+    const int width = low ? static_cast<int>(L.r) : D;
+    for (int which = 0; which < 2; ++which) {
+        const int64_t N = which == 0 ? L.Nq : L.Nk;
+        const int64_t nt = which == 0 ? L.nt_q : L.nt_k;
+        if (tile >= nt) continue;
+        const int64_t row0 = tile * 128;
+        const int rows = static_cast<int>((N - row0) < 128 ? (N - row0) : 128);
+        const void* src;
+        int64_t base, rs, cs;
+        bool vec;
+        if (low) {
+            src = which == 0 ? L.ws16_q : L.ws16_k;
+            base = (bh * N + row0) * L.ld16_qk;
+            rs = L.ld16_qk;
+            cs = 1;
+            vec = true;
+        } else {
+            const int64_t* st = which == 0 ? L.qs : L.ks;
+            src = which == 0 ? L.q : L.k;
+            base = b * st[0] + h * st[1] + row0 * st[2];
+            rs = st[2];
+            cs = st[3];
+            vec = (which == 0 ? vec_q : vec_k) != 0;
+        }
+        float x[8][8];
+        float a = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * kThreads;
+            if (i < rows * 16) {
+                const int rr = i >> 4, g = i & 15;
+                load8(src, L.in_dtype, base + rr * rs, cs, g * 8, width, vec, x[u]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) a = fmaxf(a, fabsf(x[u][k]));
+            }
+        }
+        a = block_max256(a, red);
+        const float sc = a > 0.f ? a / 448.f : 1.f;
+        if (threadIdx.x == 0) {
+            (which == 0 ? L.amax_q : L.amax_k)[bh * nt + tile] = a;
+            (which == 0 ? L.scale_q : L.scale_k)[bh * nt + tile] = sc;
+        }
+        uint8_t* dst = (which == 0 ? L.ws8_q : L.ws8_k) + (bh * N + row0) * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * kThreads;
+            if (i < rows * 16) {
+                const int rr = i >> 4, g = i & 15;
+                const float* y = x[u];
+                reinterpret_cast<uint2*>(dst + rr * 128)[g] =
+                    make_uint2(pack_e4m3x4(y[0] / sc, y[1] / sc, y[2] / sc, y[3] / sc),
+                               pack_e4m3x4(y[4] / sc, y[5] / sc, y[6] / sc, y[7] / sc));
+            }
+        }
+    }
+    if (tile < L.nt_k) {
+        float svv = 0.f;
+        for (int64_t t = 0; t < L.nt_k; ++t) svv = fmaxf(svv, L.amax_v[bh * L.nt_k + t]);
+        const float sv = svv > 0.f ? svv / 448.f : 1.f;
+        if (tile == 0 && threadIdx.x == 0) L.scale_v[bh] = sv;
+        const int64_t row0 = tile * 128;
+        const int rows = static_cast<int>((L.Nk - row0) < 128 ? (L.Nk - row0) : 128);
+        const int64_t base = b * L.vs[0] + h * L.vs[1];
+        uint8_t* dst = L.ws8_v + (bh * L.Nk + row0) * 128;
+        for (int i = threadIdx.x; i < rows * 16; i += kThreads) {
+            const int rr = i >> 4, g = i & 15;
+            float y[8];
+            load8(L.v, L.in_dtype, base + (row0 + rr) * L.vs[2], L.vs[3], g * 8, D, vec_v != 0, y);
+            reinterpret_cast<uint2*>(dst + rr * 128)[g] =
+                make_uint2(pack_e4m3x4(y[0] / sv, y[1] / sv, y[2] / sv, y[3] / sv),
+                           pack_e4m3x4(y[4] / sv, y[5] / sv, y[6] / sv, y[7] / sv));
+        }
+    }
+}
+
 int launch_cast16(const PrepLaunch& L, int skip_low_rank_qk, cudaStream_t stream) {
     const int64_t nt = ((L.Nq > L.Nk ? L.Nq : L.Nk) + kRows - 1) / kRows;
     if (nt == 0 || L.B * L.H == 0) return ADA_OK;
@@ -607,6 +716,21 @@ int launch_split(const PrepLaunch& L, cudaStream_t stream) {
 int launch_prep8(const PrepLaunch& L, cudaStream_t stream) {
     const int64_t nt = L.nt_q > L.nt_k ? L.nt_q : L.nt_k;
     if (nt == 0 || L.B * L.H == 0) return ADA_OK;
+    if (L.w_down == nullptr || L.low_src16) {
+        const int eb = L.in_dtype == ADA_F32 ? 4 : 2;
+        auto vec_ok = [&](const void* p, const int64_t* st) {
+            if (st[3] != 1 || (reinterpret_cast<uintptr_t>(p) & 15u) != 0) return 0;
+            for (int i = 0; i < 3; ++i)
+                if (((st[i] * eb) % 16) != 0) return 0;
+            return 1;
+        };
+        const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H));
+        const int vq = vec_ok(L.q, L.qs), vk = vec_ok(L.k, L.ks), vv = vec_ok(L.v, L.vs);
+        quant8_kernel<<<grid, kThreads, 0, stream>>>(L, 0, vq, vk, vv);
+        if (cudaGetLastError() != cudaSuccess) return ADA_ERR_LAUNCH;
+        quant8_kernel<<<grid, kThreads, 0, stream>>>(L, 1, vq, vk, vv);
+        return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+    }
     const size_t smem = proj_smem(L, L.w_down != nullptr && !L.low_src16);
     if (set_smem(prep8_kernel, smem) != ADA_OK) return ADA_ERR_LAUNCH;
     const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H));
