@@ -80,14 +80,21 @@ class AdaptiveTransformer(nn.Module):
     def _logits(self, h: torch.Tensor) -> torch.Tensor:
         """The tied head. A vocabulary that is not a multiple of 64 (50257)
         sends cuBLAS to a slow unaligned GEMM on the GPU, so the weight is
-        zero-padded to the next multiple of 64 rows and the extra logits are
-        dropped; the values are those of the plain Linear."""
+        zero-padded to the next multiple of 64 rows (kept until the weight
+        changes) and the logits are returned as a view of the first
+        `vocab_size` columns: the values of the plain Linear, rows 64-aligned
+        in memory (`reshape(-1, vocab_size)` and row-wise ops work as on a
+        dense tensor; copying them out would move 1.6 GB at batch 16 x 1024)."""
         w = self.head.weight
         pad = (-w.shape[0]) % 64
         if not h.is_cuda or pad == 0:
             return self.head(h)
-        wp = torch.nn.functional.pad(w, (0, 0, 0, pad))
-        return torch.matmul(h, wp.t())[..., : w.shape[0]].contiguous()
+        key = (w.data_ptr(), w._version, w.dtype, w.device)
+        if getattr(self, "_head_pad_key", None) != key:
+            self._head_pad = torch.nn.functional.pad(w.detach(), (0, 0, 0, pad))
+            self._head_pad_key = key
+        wp = self._head_pad if not torch.is_grad_enabled() else torch.nn.functional.pad(w, (0, 0, 0, pad))
+        return torch.matmul(h, wp.t())[..., : w.shape[0]]
 
     def get_attention_statistics(self):
         stats = []

@@ -1,0 +1,32 @@
+"""The decoder hosting AdaAttention in the GPT-2-small workload: its tied
+head (padded weight, logits as a view) against the plain Linear."""
+
+import pytest
+import torch
+
+from adaattn_b200.host_model import AdaptiveTransformer
+
+pytestmark = pytest.mark.gpu
+
+
+def test_tied_head_logits_match_linear(cuda_device):
+    torch.manual_seed(0)
+    m = AdaptiveTransformer(vocab_size=1000, embed_dim=128, num_heads=2, num_layers=2, ff_dim=256,
+                            max_seq_len=64)
+    m.init_gpt2_weights()
+    m = m.to(cuda_device).bfloat16().eval()
+    ids = torch.randint(0, 1000, (2, 64), device=cuda_device)
+    h = torch.randn(2, 64, 128, device=cuda_device).bfloat16()
+    with torch.no_grad():
+        got = m._logits(h)
+        want = torch.nn.functional.linear(h.float(), m.head.weight.float())
+        assert got.shape == (2, 64, 1000)
+        err = (got.float() - want).abs().max().item()
+        assert err <= 2.0 ** -7 * want.abs().max().item() + 1e-3
+        flat = got.reshape(-1, 1000)  # row-wise use of the view
+        assert torch.equal(flat.argmax(-1), got.argmax(-1).reshape(-1))
+        logits = m(ids)
+        assert logits.shape == (2, 64, 1000) and torch.isfinite(logits.float()).all()
+        # a changed weight is picked up (the padded copy is rebuilt)
+        m.head.weight.mul_(2.0)
+        assert torch.allclose(m._logits(h).float(), 2.0 * got.float(), rtol=0, atol=1e-2 * got.float().abs().max().item())
