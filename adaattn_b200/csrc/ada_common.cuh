@@ -440,6 +440,37 @@ __device__ __forceinline__ void unpack_f16x2(uint32_t v, float& lo, float& hi) {
         : "=f"(lo), "=f"(hi)
         : "r"(v));
 }
+// Eight consecutive values x[row, c0 .. c0+7] as fp32, zero from column
+// `width` on. `vec`: unit column stride and 16-byte aligned rows.
+__device__ __forceinline__ void load8(const void* x, int dt, int64_t row_base, int64_t col_stride, int c0,
+                                      int width, bool vec, float (&v)[8]) {
+    if (vec && c0 + 8 <= width) {
+        const int64_t e = row_base + c0;
+        if (dt == ADA_F32) {
+            const float4 a = reinterpret_cast<const float4*>(x)[e / 4];
+            const float4 c = reinterpret_cast<const float4*>(x)[e / 4 + 1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+        } else {
+            const uint4 a = reinterpret_cast<const uint4*>(x)[e / 8];
+            const uint32_t w4[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (dt == ADA_BF16) {
+                    v[2 * k] = __uint_as_float(w4[k] << 16);
+                    v[2 * k + 1] = __uint_as_float(w4[k] & 0xffff0000u);
+                } else {
+                    unpack_f16x2(w4[k], v[2 * k], v[2 * k + 1]);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            v[k] = (c0 + k < width) ? load_as_f32(x, row_base + (c0 + k) * col_stride, dt) : 0.f;
+    }
+}
+
 // Four fp32 values -> four E4M3 bytes (saturating), first value in the low byte.
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
     __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);

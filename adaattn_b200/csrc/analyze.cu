@@ -25,6 +25,7 @@ struct StatsArgs {
     int64_t qs[4], ks[4];
     float scale, eps, log_s;
     int S, stride;
+    int vec;            // 16-bit q and k with unit column stride and 16-byte aligned rows, D % 8 == 0
     float* head_stats;  // [B*H*4]
     float* head_sum;    // [B*H]  sum over sampled rows of the normalised row entropy
 };
@@ -49,11 +50,55 @@ __global__ void __launch_bounds__(kThreads) analyze_stats_kernel(StatsArgs a) {
     }
     const int64_t qbase = b * a.qs[0] + h * a.qs[1];
     const int64_t kbase = b * a.ks[0] + h * a.ks[1];
-    for (int idx = tid; idx < S * D; idx += kThreads) {
-        const int r = idx / D, d = idx - r * D;
-        const int64_t row = static_cast<int64_t>(r) * a.stride;
-        sq[r * ld + d] = load_as_f32(a.q, qbase + row * a.qs[2] + d * a.qs[3], a.dtype);
-        sk[r * ld + d] = load_as_f32(a.k, kbase + row * a.ks[2] + d * a.ks[3], a.dtype);
+    if (a.vec) {
+        // 16-byte loads, all of this thread's in flight before the first use
+        // (S * D / 8 <= 1024 groups: at most 4 per thread and tensor).
+        const int g = D >> 3;
+        const int n = S * g;
+        uint4 vq[4], vk[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int idx = tid + u * kThreads;
+            if (idx < n) {
+                const int r = idx / g, c = (idx - r * g) * 8;
+                const int64_t row = static_cast<int64_t>(r) * a.stride;
+                vq[u] = reinterpret_cast<const uint4*>(a.q)[(qbase + row * a.qs[2] + c) / 8];
+                vk[u] = reinterpret_cast<const uint4*>(a.k)[(kbase + row * a.ks[2] + c) / 8];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int idx = tid + u * kThreads;
+            if (idx < n) {
+                const int r = idx / g, c = (idx - r * g) * 8;
+                const uint32_t wq[4] = {vq[u].x, vq[u].y, vq[u].z, vq[u].w};
+                const uint32_t wk[4] = {vk[u].x, vk[u].y, vk[u].z, vk[u].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float q0, q1, k0, k1;
+                    if (a.dtype == ADA_BF16) {
+                        q0 = __uint_as_float(wq[i] << 16);
+                        q1 = __uint_as_float(wq[i] & 0xffff0000u);
+                        k0 = __uint_as_float(wk[i] << 16);
+                        k1 = __uint_as_float(wk[i] & 0xffff0000u);
+                    } else {
+                        unpack_f16x2(wq[i], q0, q1);
+                        unpack_f16x2(wk[i], k0, k1);
+                    }
+                    sq[r * ld + c + 2 * i] = q0;
+                    sq[r * ld + c + 2 * i + 1] = q1;
+                    sk[r * ld + c + 2 * i] = k0;
+                    sk[r * ld + c + 2 * i + 1] = k1;
+                }
+            }
+        }
+    } else {
+        for (int idx = tid; idx < S * D; idx += kThreads) {
+            const int r = idx / D, d = idx - r * D;
+            const int64_t row = static_cast<int64_t>(r) * a.stride;
+            sq[r * ld + d] = load_as_f32(a.q, qbase + row * a.qs[2] + d * a.qs[3], a.dtype);
+            sk[r * ld + d] = load_as_f32(a.k, kbase + row * a.ks[2] + d * a.ks[3], a.dtype);
+        }
     }
     __syncthreads();
 
@@ -361,6 +406,16 @@ int launch_analyze(const AnalyzeLaunch& L, cudaStream_t stream) {
     a.log_s = static_cast<float>(L.log_s);
     a.head_stats = L.head_stats;
     a.head_sum = L.head_sum;
+    {
+        auto rows16 = [](const void* p, const int64_t* st) {
+            if (st[3] != 1 || (reinterpret_cast<uintptr_t>(p) & 15u) != 0) return false;
+            for (int i = 0; i < 3; ++i)
+                if (((st[i] * 2) % 16) != 0) return false;
+            return true;
+        };
+        a.vec = (L.dtype == ADA_F16 || L.dtype == ADA_BF16) && (L.D % 8) == 0 && rows16(L.q, L.qs) &&
+                rows16(L.k, L.ks);
+    }
     const size_t smem = static_cast<size_t>(2 * kSample * (L.D + 1)) * sizeof(float);
     if (smem > 48 * 1024) {
         if (cudaFuncSetAttribute(analyze_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
