@@ -210,15 +210,41 @@ class AdaAttention(nn.Module):
         b, nq, _ = query.shape
         nk = key.shape[1]
         h, d = self.num_heads, self.head_dim
-        q = self.q_proj(query).view(b, nq, h, d).transpose(1, 2)
-        k = self.k_proj(key).view(b, nk, h, d).transpose(1, 2)
-        v = self.v_proj(value).view(b, nk, h, d).transpose(1, 2)
+        if query is key and key is value:
+            # Self-attention: one GEMM against the stacked q/k/v weights
+            # (same values as the three Linears); q, k, v are column views.
+            w, bias = self._stacked_qkv()
+            qkv = torch.nn.functional.linear(query, w, bias)
+            e = self.embed_dim
+            q, k, v = (qkv[..., i * e:(i + 1) * e].view(b, nq, h, d).transpose(1, 2) for i in range(3))
+        else:
+            q = self.q_proj(query).view(b, nq, h, d).transpose(1, 2)
+            k = self.k_proj(key).view(b, nk, h, d).transpose(1, 2)
+            v = self.v_proj(value).view(b, nk, h, d).transpose(1, 2)
         merged = torch.empty(b, nq, h, d, dtype=q.dtype, device=q.device)
         attn_out, _ = self.attention_core(q, k, v, attention_mask, out=merged.transpose(1, 2))
         if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
             merged = _ForwardOnly.apply(merged, q, k, v)
         output = self.resid_dropout(self.out_proj(merged.view(b, nq, self.embed_dim)))
         return output, None
+
+    def _stacked_qkv(self) -> Tuple[Tensor, Optional[Tensor]]:
+        """[3E, E] weight and [3E] bias of q_proj, k_proj, v_proj stacked; kept
+        between calls (outside the state dict) until a parameter changes,
+        rebuilt on every call when autograd tracks the parameters."""
+        ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+        bs = (self.q_proj.bias, self.k_proj.bias, self.v_proj.bias)
+        has_bias = all(t is not None for t in bs)
+        if torch.is_grad_enabled() and any(t.requires_grad for t in ws + (bs if has_bias else ())):
+            return torch.cat(ws), (torch.cat(bs) if has_bias else None)
+        params = ws + (bs if has_bias else ())
+        key = tuple((t.data_ptr(), t._version, t.dtype, t.device) for t in params)
+        if getattr(self, "_qkv_key", None) != key:
+            with torch.no_grad():
+                self._qkv_w = torch.cat(ws)
+                self._qkv_b = torch.cat(bs) if has_bias else None
+            self._qkv_key = key
+        return self._qkv_w, self._qkv_b
 
     def attention_core(self, q: Tensor, k: Tensor, v: Tensor,
                        attention_mask: Optional[Tensor] = None, out: Optional[Tensor] = None

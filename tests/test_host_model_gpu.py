@@ -30,3 +30,23 @@ def test_tied_head_logits_match_linear(cuda_device):
         # a changed weight is picked up (the padded copy is rebuilt)
         m.head.weight.mul_(2.0)
         assert torch.allclose(m._logits(h).float(), 2.0 * got.float(), rtol=0, atol=1e-2 * got.float().abs().max().item())
+
+
+def test_self_attention_stacked_projection_matches_separate(cuda_device):
+    """Self-attention (query is key is value) projects through one GEMM with
+    the stacked q/k/v weights; the result equals the three-Linear path."""
+    from adaattn_b200 import AdaAttention
+    torch.manual_seed(1)
+    m = AdaAttention(embed_dim=256, num_heads=4).to(cuda_device).bfloat16().eval()
+    x = (torch.randn(2, 200, 256, device=cuda_device) * 0.5).bfloat16()
+    with torch.no_grad():
+        fused, _ = m(x, x, x)
+        sep, _ = m(x, x.clone(), x.clone())
+        err = (fused.float() - sep.float()).abs().max().item()
+        assert err <= 2.0 ** -7 * max(1.0, sep.float().abs().max().item())
+        # a parameter update reaches the stacked copy
+        m.k_proj.weight.mul_(0.5)
+        fused2, _ = m(x, x, x)
+        sep2, _ = m(x, x.clone(), x.clone())
+        err2 = (fused2.float() - sep2.float()).abs().max().item()
+        assert err2 <= 2.0 ** -7 * max(1.0, sep2.float().abs().max().item())
