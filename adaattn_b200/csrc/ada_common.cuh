@@ -471,6 +471,14 @@ __device__ __forceinline__ void load8(const void* x, int dt, int64_t row_base, i
     }
 }
 
+// x / d from the correctly rounded reciprocal inv_d = 1/d: q0 = x * inv_d,
+// then one residual step q0 + (x - q0 * d) * inv_d with the residual formed
+// exactly by an fma (Markstein's correction; gives the correctly rounded
+// quotient for normal operands). For many divisions by one d.
+__device__ __forceinline__ float div_by(float x, float d, float inv_d) {
+    const float q0 = x * inv_d;
+    return fmaf(fmaf(-q0, d, x), inv_d, q0);
+}
 // Four fp32 values -> four E4M3 bytes (saturating), first value in the low byte.
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
     __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);

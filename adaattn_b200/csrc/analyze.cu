@@ -31,11 +31,13 @@ struct StatsArgs {
 };
 
 __global__ void __launch_bounds__(kThreads) analyze_stats_kernel(StatsArgs a) {
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     const int D = static_cast<int>(a.D);
-    const int ld = D + 1;
+    const int DP = (D + 3) & ~3;  // columns D..DP-1 hold zeros
+    const int ld = DP + 4;        // 16-byte rows, staggered banks
     float* sq = sm;
     float* sk = sm + kSample * ld;
+    float* ss = sk + kSample * ld;  // [kSample][kSample + 1] raw scores
     __shared__ unsigned int s_max_score, s_max_prob;
     __shared__ float s_rows[kSample];
 
@@ -100,6 +102,43 @@ __global__ void __launch_bounds__(kThreads) analyze_stats_kernel(StatsArgs a) {
             sk[r * ld + d] = load_as_f32(a.k, kbase + row * a.ks[2] + d * a.ks[3], a.dtype);
         }
     }
+    for (int idx = tid; idx < S * (DP - D); idx += kThreads) {
+        const int r = idx / (DP - D), d = D + idx - r * (DP - D);
+        sq[r * ld + d] = 0.f;
+        sk[r * ld + d] = 0.f;
+    }
+    __syncthreads();
+    // q k^T of the sample: each thread a 4 x 4 block (rows 4*ty + i, columns
+    // tx + 16*j), 16-byte shared loads; every score is one fma chain over
+    // d = 0, 1, ..., D-1 (the zero padding adds nothing).
+    {
+        const int ty = tid >> 4, tx = tid & 15;
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+        for (int d = 0; d < DP; d += 4) {
+            float4 qa[4], kb[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qa[i] = *reinterpret_cast<const float4*>(sq + (ty * 4 + i) * ld + d);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kb[j] = *reinterpret_cast<const float4*>(sk + (tx + 16 * j) * ld + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc[i][j] = fmaf(qa[i].x, kb[j].x, acc[i][j]);
+                    acc[i][j] = fmaf(qa[i].y, kb[j].y, acc[i][j]);
+                    acc[i][j] = fmaf(qa[i].z, kb[j].z, acc[i][j]);
+                    acc[i][j] = fmaf(qa[i].w, kb[j].w, acc[i][j]);
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ss[(ty * 4 + i) * (kSample + 1) + tx + 16 * j] = acc[i][j];
+    }
     __syncthreads();
 
     // Thread layout: 4 consecutive lanes own one sample row, 16 columns each.
@@ -108,18 +147,7 @@ __global__ void __launch_bounds__(kThreads) analyze_stats_kernel(StatsArgs a) {
     const bool row_ok = r < S;
     float sc[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) sc[j] = 0.f;
-    if (row_ok) {
-        const float* qr = sq + r * ld;
-        for (int d = 0; d < D; ++d) {
-            const float qv = qr[d];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int col = c0 + j;
-                if (col < S) sc[j] = fmaf(qv, sk[col * ld + d], sc[j]);
-            }
-        }
-    }
+    for (int j = 0; j < 16; ++j) sc[j] = ss[r * (kSample + 1) + c0 + j];
     // scores = round(round(q k^T) * scale); track max |score|.
     float local_max_abs = 0.f;
     float row_max = -INFINITY;
@@ -416,7 +444,8 @@ int launch_analyze(const AnalyzeLaunch& L, cudaStream_t stream) {
         a.vec = (L.dtype == ADA_F16 || L.dtype == ADA_BF16) && (L.D % 8) == 0 && rows16(L.q, L.qs) &&
                 rows16(L.k, L.ks);
     }
-    const size_t smem = static_cast<size_t>(2 * kSample * (L.D + 1)) * sizeof(float);
+    const size_t smem = static_cast<size_t>(2 * kSample * (((L.D + 3) & ~3) + 4) + kSample * (kSample + 1)) *
+                        sizeof(float);
     if (smem > 48 * 1024) {
         if (cudaFuncSetAttribute(analyze_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem)) != cudaSuccess)

@@ -604,15 +604,18 @@ __global__ void __launch_bounds__(kThreads) quant8_kernel(const __grid_constant_
             (which == 0 ? L.scale_q : L.scale_k)[bh * nt + tile] = sc;
         }
         uint8_t* dst = (which == 0 ? L.ws8_q : L.ws8_k) + (bh * N + row0) * 128;
+        const float isc = 1.f / sc;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             const int i = threadIdx.x + u * kThreads;
             if (i < rows * 16) {
                 const int rr = i >> 4, g = i & 15;
                 const float* y = x[u];
-                reinterpret_cast<uint2*>(dst + rr * 128)[g] =
-                    make_uint2(pack_e4m3x4(y[0] / sc, y[1] / sc, y[2] / sc, y[3] / sc),
-                               pack_e4m3x4(y[4] / sc, y[5] / sc, y[6] / sc, y[7] / sc));
+                reinterpret_cast<uint2*>(dst + rr * 128)[g] = make_uint2(
+                    pack_e4m3x4(div_by(y[0], sc, isc), div_by(y[1], sc, isc), div_by(y[2], sc, isc),
+                                div_by(y[3], sc, isc)),
+                    pack_e4m3x4(div_by(y[4], sc, isc), div_by(y[5], sc, isc), div_by(y[6], sc, isc),
+                                div_by(y[7], sc, isc)));
             }
         }
     }
@@ -625,13 +628,16 @@ __global__ void __launch_bounds__(kThreads) quant8_kernel(const __grid_constant_
         const int rows = static_cast<int>((L.Nk - row0) < 128 ? (L.Nk - row0) : 128);
         const int64_t base = b * L.vs[0] + h * L.vs[1];
         uint8_t* dst = L.ws8_v + (bh * L.Nk + row0) * 128;
+        const float isv = 1.f / sv;
         for (int i = threadIdx.x; i < rows * 16; i += kThreads) {
             const int rr = i >> 4, g = i & 15;
             float y[8];
             load8(L.v, L.in_dtype, base + (row0 + rr) * L.vs[2], L.vs[3], g * 8, D, vec_v != 0, y);
-            reinterpret_cast<uint2*>(dst + rr * 128)[g] =
-                make_uint2(pack_e4m3x4(y[0] / sv, y[1] / sv, y[2] / sv, y[3] / sv),
-                           pack_e4m3x4(y[4] / sv, y[5] / sv, y[6] / sv, y[7] / sv));
+            reinterpret_cast<uint2*>(dst + rr * 128)[g] = make_uint2(
+                pack_e4m3x4(div_by(y[0], sv, isv), div_by(y[1], sv, isv), div_by(y[2], sv, isv),
+                            div_by(y[3], sv, isv)),
+                pack_e4m3x4(div_by(y[4], sv, isv), div_by(y[5], sv, isv), div_by(y[6], sv, isv),
+                            div_by(y[7], sv, isv)));
         }
     }
 }
