@@ -136,6 +136,7 @@ struct PrepLaunch {
     // heads), v [B*H][N][128].
     uint32_t split_mask;      // precision codes served this way (FP32) or 0
     int split_low, split_dense;  // which FP32 heads (low rank / dense) are served
+    int split_qk_low, split_qk_dense;  // 1: their q/k are scaled into wss_q/wss_k (else read in place)
     int64_t split_ld;
     uint16_t* wss_q;
     uint16_t* wss_k;
@@ -157,7 +158,7 @@ struct ProjLaunch {
     int64_t B, H, Nq, Nk;
     int D, r, r_pad;
     uint32_t tc16_mask, f16_mask, fp32_mask;
-    uint32_t fp8_mask;  // E4M3 heads: q_low/k_low go to the 16-bit region in the input dtype
+    uint32_t in16_mask;  // E4M3 heads and FP32 heads on the tensor cores: q_low/k_low to the 16-bit region in the input dtype
     void* ws16_q;
     void* ws16_k;
     int64_t ld16;
@@ -181,7 +182,7 @@ int launch_split(const PrepLaunch& L, cudaStream_t stream);
 // --- tensor-core FMHA (tcgen05) -----------------------------------------------
 struct TcLaunch {
     CUtensorMap tq, tk, tv;
-    int elt;          // 0 f16, 1 bf16, 2 e4m3, 3 fp32 heads: scaled fp16 operands, P as fp16 hi + lo
+    int elt;          // 0 f16, 1 bf16, 2 e4m3; FP32 heads (P as fp16 hi + lo, fp16 V): 3 fp16 q/k, 4 bf16 q/k
     int dqk, dv;      // operand widths (64 or 128)
     int64_t B, H, Nq, Nk;
     int dv_out;       // real value width stored
@@ -196,9 +197,9 @@ struct TcLaunch {
     int causal;
     MaskView mask;
     HeadSelect sel;
-    const float* q_scale;  // e4m3 and split: [B,H,nt_q]
-    const float* k_scale;  // e4m3 and split: [B,H,nt_k]
-    const float* v_scale;  // e4m3 and split: [B,H]
+    const float* q_scale;  // e4m3, and FP32 heads with scaled q/k: [B,H,nt_q] (else nullptr)
+    const float* k_scale;  // e4m3, and FP32 heads with scaled q/k: [B,H,nt_k] (else nullptr)
+    const float* v_scale;  // e4m3 and FP32 heads: [B,H]
     int64_t nt_q, nt_k;
     int* work_counter;  // zeroed work-item counter (dynamic scheduling), or nullptr (static striding)
     unsigned int* status;

@@ -222,8 +222,11 @@ struct Plan {
     bool need16, need32, need8;
     bool split;          // some FP32 heads run on the tensor cores (scaled fp16 operands, split P)
     bool split_low, split_dense;
+    bool split_low_direct, split_dense_direct;  // q/k read in place (16-bit region / inputs), not scaled
+    bool split_scaled;   // some FP32 heads' q/k are scaled into the split q/k region
     int64_t split_ld;    // row width of the split q/k region
     bool proj_tc_shape;  // low-rank projection can run on the tensor cores
+    bool proj_tc;        // ... and will (the weight is 16-byte aligned)
     int64_t nt_q, nt_k;
     size_t off16q, off16k, off16v, off32q, off32k, off8q, off8k, off8v;
     size_t off_amax_q, off_amax_k, off_amax_v, off_sq, off_sk, off_sv;
@@ -309,21 +312,34 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
     }
     P->need32 = ((P->possible & P->fp32_mask) != 0) && P->low_possible;
     P->need8 = (P->possible & P->fp8_mask) != 0;
+    P->proj_tc_shape = P->low_possible && P->direct_ok &&
+                       ((P->D == 128 && P->r <= 128) || (P->D == 64 && P->r <= 64));
+    P->proj_tc = P->proj_tc_shape && (reinterpret_cast<uintptr_t>(w_down->data) & 15u) == 0;
     // FP32 heads of 16-bit inputs (dense, or low rank with r <= 64) run
-    // fp32-accurate on the tensor cores (scaled fp16 operands, split P);
-    // wider ranks and fp32 inputs stay on the CUDA cores.
+    // fp32-accurate on the tensor cores (exact 16-bit q/k products, split P);
+    // wider ranks and fp32 inputs stay on the CUDA cores. Their q/k are read
+    // in place when the tensor-core projection writes q_low/k_low to the
+    // 16-bit region (low rank) or the inputs are TMA-readable (dense), else
+    // scaled into a region of their own.
     {
         const bool in16 = P->in_dtype == ADA_F16 || P->in_dtype == ADA_BF16;
         const bool fp32 = (P->possible & P->fp32_mask) != 0;
-        P->split_low = in16 && P->need32 && P->r <= 64;
+        P->split_low = in16 && fp32 && P->low_possible && P->r <= 64;
         P->split_dense = in16 && fp32 && P->dense_possible;
+        P->split_low_direct = P->split_low && P->proj_tc;
+        P->split_dense_direct = P->split_dense && P->direct_ok;
         P->split = P->split_low || P->split_dense;
-        P->split_ld = P->split_dense ? P->dqk_dense : 64;
+        const bool scaled_low = P->split_low && !P->split_low_direct;
+        const bool scaled_dense = P->split_dense && !P->split_dense_direct;
+        P->split_scaled = scaled_low || scaled_dense;
+        P->split_ld = scaled_dense ? P->dqk_dense : 64;
+        if (P->split_low_direct) {
+            P->need32 = false;
+            P->need16 = true;
+        }
     }
     // E4M3 low-rank heads take their projection from the tensor-core kernel,
     // which writes q_low/k_low into the 16-bit region.
-    P->proj_tc_shape = P->low_possible && P->direct_ok &&
-                       ((P->D == 128 && P->r <= 128) || (P->D == 64 && P->r <= 64));
     if (P->need8 && P->proj_tc_shape) P->need16 = true;
     P->nt_q = (P->Nq + 127) / 128;
     P->nt_k = (P->Nk + 127) / 128;
@@ -344,10 +360,11 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
         off = align256(off + static_cast<size_t>(BH * P->Nk * P->r) * 4);
     }
     if (P->split) {
+        const int64_t lq = P->split_scaled ? P->split_ld : 0;
         P->offs_q = off;
-        off = align256(off + static_cast<size_t>(BH * P->Nq * P->split_ld) * 2);
+        off = align256(off + static_cast<size_t>(BH * P->Nq * lq) * 2);
         P->offs_k = off;
-        off = align256(off + static_cast<size_t>(BH * P->Nk * P->split_ld) * 2);
+        off = align256(off + static_cast<size_t>(BH * P->Nk * lq) * 2);
         P->offs_v = off;
         off = align256(off + static_cast<size_t>(BH * P->Nk * 128) * 2);
         P->offs_sq = off;
@@ -593,8 +610,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
     // Low-rank q/k projection on the tensor cores when the inputs are 16-bit
     // and TMA-readable; the SIMT projection kernels cover every other case.
     const int r_pad = P.low_possible ? pad_width(P.r) : 0;
-    const bool proj_tc = P.proj_tc_shape && (P.need16 || P.need32) &&
-                         (reinterpret_cast<uintptr_t>(w_down->data) & 15u) == 0;
+    const bool proj_tc = P.proj_tc && (P.need16 || P.need32);
     if (P.need16) {
         pl.ws16_q = ws + P.off16q;
         pl.ws16_k = ws + P.off16k;
@@ -629,7 +645,8 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         pj.r_pad = r_pad;
         // Only precisions whose operand region exists are written.
         pj.tc16_mask = P.need16 ? (P.tc16_mask & P.possible) : 0u;
-        pj.fp8_mask = P.need8 ? (P.fp8_mask & P.possible) : 0u;
+        pj.in16_mask = (P.need8 ? (P.fp8_mask & P.possible) : 0u) |
+                       (P.split_low_direct ? (P.fp32_mask & P.possible) : 0u);
         pj.f16_mask = P.f16_mask;
         pj.fp32_mask = P.need32 ? (P.fp32_mask & P.possible) : 0u;
         pj.ws16_q = pl.ws16_q;
@@ -642,7 +659,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         // Outputs through TMA stores when the rank pads to 64 columns.
         if (r_pad == 64 && P.Nq > 0 && P.Nk > 0) {
             const int64_t BH = P.B * P.H;
-            if ((pj.tc16_mask | pj.fp8_mask) != 0u) {
+            if ((pj.tc16_mask | pj.in16_mask) != 0u) {
                 const int64_t l = P.ld16_qk;
                 if ((rc = make_map_3d(&pj.to16_q, pj.ws16_q, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, l, P.Nq, BH, l,
                                       P.Nq * l, 64)) ||
@@ -680,6 +697,8 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         pl.split_mask = P.fp32_mask;
         pl.split_low = P.split_low ? 1 : 0;
         pl.split_dense = P.split_dense ? 1 : 0;
+        pl.split_qk_low = (P.split_low && !P.split_low_direct) ? 1 : 0;
+        pl.split_qk_dense = (P.split_dense && !P.split_dense_direct) ? 1 : 0;
         pl.split_ld = P.split_ld;
         pl.wss_q = reinterpret_cast<uint16_t*>(ws + P.offs_q);
         pl.wss_k = reinterpret_cast<uint16_t*>(ws + P.offs_k);
@@ -785,19 +804,37 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         if (!(low ? P.split_low : P.split_dense)) continue;
         TcLaunch L;
         base_tc(L);
-        L.elt = 3;
+        const bool direct = low ? P.split_low_direct : P.split_dense_direct;
+        L.elt = (direct && P.in_dtype == ADA_BF16) ? 4 : 3;
         L.round_dtype = ADA_F32;
         L.sel = HeadSelect{decisions, P.fp32_mask, low};
-        L.dqk = low ? 64 : P.dqk_dense;
         L.dv = 128;
-        L.q_scale = reinterpret_cast<float*>(ws + P.offs_sq);
-        L.k_scale = reinterpret_cast<float*>(ws + P.offs_sk);
         L.v_scale = reinterpret_cast<float*>(ws + P.offs_sv);
-        const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-        const int64_t l = P.split_ld;
-        if ((rc = make_map(&L.tq, ws + P.offs_q, dt, 2, L.dqk, P.Nq, P.H, P.B, l, P.Nq * l, P.H * P.Nq * l)) ||
-            (rc = make_map(&L.tk, ws + P.offs_k, dt, 2, L.dqk, P.Nk, P.H, P.B, l, P.Nk * l, P.H * P.Nk * l)) ||
-            (rc = make_map(&L.tv, ws + P.offs_v, dt, 2, 128, P.Nk, P.H, P.B, 128, P.Nk * 128, P.H * P.Nk * 128)))
+        const CUtensorMapDataType f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        if (direct && low) {
+            // q_low/k_low in the 16-bit region, inputs' dtype, 64 columns
+            L.dqk = 64;
+            const CUtensorMapDataType dt = tma_dtype(P.in_dtype);
+            const int64_t l = P.ld16_qk;
+            if ((rc = make_map(&L.tq, ws + P.off16q, dt, 2, 64, P.Nq, P.H, P.B, l, P.Nq * l, P.H * P.Nq * l)) ||
+                (rc = make_map(&L.tk, ws + P.off16k, dt, 2, 64, P.Nk, P.H, P.B, l, P.Nk * l, P.H * P.Nk * l)))
+                return rc;
+        } else if (direct) {
+            L.dqk = static_cast<int>(P.D);
+            const CUtensorMapDataType dt = tma_dtype(P.in_dtype);
+            if ((rc = make_map(&L.tq, q->data, dt, 2, P.D, P.Nq, P.H, P.B, q->stride[2], q->stride[1], q->stride[0])) ||
+                (rc = make_map(&L.tk, k->data, dt, 2, P.D, P.Nk, P.H, P.B, k->stride[2], k->stride[1], k->stride[0])))
+                return rc;
+        } else {
+            L.dqk = low ? 64 : P.dqk_dense;
+            L.q_scale = reinterpret_cast<float*>(ws + P.offs_sq);
+            L.k_scale = reinterpret_cast<float*>(ws + P.offs_sk);
+            const int64_t l = P.split_ld;
+            if ((rc = make_map(&L.tq, ws + P.offs_q, f16, 2, L.dqk, P.Nq, P.H, P.B, l, P.Nq * l, P.H * P.Nq * l)) ||
+                (rc = make_map(&L.tk, ws + P.offs_k, f16, 2, L.dqk, P.Nk, P.H, P.B, l, P.Nk * l, P.H * P.Nk * l)))
+                return rc;
+        }
+        if ((rc = make_map(&L.tv, ws + P.offs_v, f16, 2, 128, P.Nk, P.H, P.B, 128, P.Nk * 128, P.H * P.Nk * 128)))
             return rc;
         if (L.dqk == 128 && P.D == 128 && (out->dtype == ADA_F16 || out->dtype == ADA_BF16) && out->stride[3] == 1 &&
             out_vec_bytes(out) >= 16) {

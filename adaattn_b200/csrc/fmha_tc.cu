@@ -77,17 +77,19 @@ struct TcCfg {
     static constexpr int NSTAGE = NSTAGE_RAW > 8 ? 8 : NSTAGE_RAW;
     static_assert(NSTAGE >= 2, "ring too small");
     static constexpr int MMA_K = (ELT == 2) ? 32 : 16;   // elements per MMA k-step
-    // ELT 3: FP32 heads of 16-bit inputs. q, k (or q_low, k_low, rounded to
-    // the inputs' dtype by the projection) and v are exact in fp16 once
-    // scaled by powers of two, so Q·Kᵀ and the fp32 accumulation are exact
-    // up to the accumulator; P keeps fp32 accuracy as an fp16 sum hi + lo
-    // (TMEM columns 0..63 and 64..127), each part multiplied into V.
-    static constexpr bool SPLIT = ELT == 3;
+    // ELT 3 / 4: FP32 heads of 16-bit inputs. q, k (or q_low, k_low, rounded
+    // to the inputs' dtype by the projection) are read as fp16 (3) or bf16 (4)
+    // -- in place, or scaled by powers of two into fp16 -- so Q·Kᵀ products
+    // are exact and only the fp32 accumulation rounds; v is scaled into fp16
+    // (exact) and P keeps fp32 accuracy as an fp16 sum hi + lo (TMEM columns
+    // 0..63 and 64..127 of S), each part multiplied into V.
+    static constexpr bool SPLIT = ELT == 3 || ELT == 4;
     static_assert(!SPLIT || DV == 128, "split operands: 128-column v rows");
     static constexpr int KSTEP_BYTES = MMA_K * EB;        // 32 bytes either way
     static constexpr int P_COLS = BN * EB / 4;            // TMEM columns holding P
-    static constexpr uint32_t FMT = (ELT == 1) ? 1u : 0u; // bf16 = 1, f16 = 0, e4m3 = 0
-    static constexpr uint32_t IDESC_QK = make_idesc(FMT, FMT, 0, 0, 128, BN);
+    static constexpr uint32_t FMT = (ELT == 1) ? 1u : 0u; // P·V operands: bf16 = 1, f16 = 0, e4m3 = 0
+    static constexpr uint32_t FMT_QK = (ELT == 1 || ELT == 4) ? 1u : 0u;  // Q·Kᵀ operands
+    static constexpr uint32_t IDESC_QK = make_idesc(FMT_QK, FMT_QK, 0, 0, 128, BN);
     static constexpr uint32_t IDESC_PV = make_idesc(FMT, FMT, 0, 1, 128, DV);
     static constexpr int SMEM_BYTES = 2 * QBUF_BYTES + NSTAGE * STAGE_BYTES + 1024 + 512;
 };
@@ -457,7 +459,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             const int qrow = tile_r0 + row;
             const int Nk = static_cast<int>(L.Nk);
             float sq = 1.f;
-            if constexpr (ELT >= 2) sq = L.q_scale[w.bh * L.nt_q + (w.qtp * 2 + t)];
+            if constexpr (ELT >= 2)
+                if (L.q_scale != nullptr) sq = L.q_scale[w.bh * L.nt_q + (w.qtp * 2 + t)];
             float m_run = -INFINITY;
             float l_run = 0.f;
             for (int j = 0; j < nt; ++j) {
@@ -486,7 +489,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     }
                 }
                 float sl2 = scale_log2;
-                if constexpr (ELT >= 2) sl2 *= sq * L.k_scale[w.bh * L.nt_k + j];
+                if constexpr (ELT >= 2)
+                    if (L.k_scale != nullptr) sl2 *= sq * L.k_scale[w.bh * L.nt_k + j];
                 const int kv0 = j * 128;
                 const bool edge = (kv0 + 128 > Nk) || (causal && kv0 + 127 > tile_r0);
                 if (edge) {
@@ -639,7 +643,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             // ---- epilogue: O / l, rounded like the reference's result, stored ----
             float post = 1.f / l_run;
             if constexpr (ELT == 2) post *= L.v_scale[w.bh] * (1.f / 448.f);
-            if constexpr (ELT == 3) post *= L.v_scale[w.bh] * (1.f / kSplitPScale);
+            if constexpr (C::SPLIT) post *= L.v_scale[w.bh] * (1.f / kSplitPScale);
             const bool row_ok = qrow < L.Nq;
             uint8_t* orow = reinterpret_cast<uint8_t*>(L.out);
             const int64_t obase = w.b * L.os[0] + w.h * L.os[1] + static_cast<int64_t>(qrow) * L.os[2];
@@ -792,6 +796,11 @@ int launch_fmha_tc(const TcLaunch& L, cudaStream_t stream) {
     if (L.elt == 3) {
         if (L.dqk == 128 && L.dv == 128) return launch_variant<3, 128, 128>(L, stream);
         if (L.dqk == 64 && L.dv == 128) return launch_variant<3, 64, 128>(L, stream);
+        return ADA_ERR_UNSUPPORTED;
+    }
+    if (L.elt == 4) {
+        if (L.dqk == 128 && L.dv == 128) return launch_variant<4, 128, 128>(L, stream);
+        if (L.dqk == 64 && L.dv == 128) return launch_variant<4, 64, 128>(L, stream);
         return ADA_ERR_UNSUPPORTED;
     }
     if (L.elt == 2) {

@@ -457,7 +457,8 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const __grid_constant__
     const int width = kind == 1 ? static_cast<int>(L.r) : static_cast<int>(L.D);
     const int wout = kind == 1 ? 64 : L.dqk_dense;
     const int groups = wout / 8;
-    for (int which = 0; which < 2; ++which) {
+    const bool scale_qk = kind == 1 ? L.split_qk_low != 0 : L.split_qk_dense != 0;
+    for (int which = 0; which < (scale_qk ? 2 : 0); ++which) {
         const int64_t N = which == 0 ? L.Nq : L.Nk;
         const int64_t nt = which == 0 ? L.nt_q : L.nt_k;
         if (tile >= nt) continue;

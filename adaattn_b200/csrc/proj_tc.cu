@@ -47,7 +47,7 @@ __device__ __forceinline__ bool proj_item(const ProjLaunch& L, int64_t it, int n
     w->tile = rem < ntq ? rem : rem - ntq;
     int low;
     get_decision(L.dec, w->bh, prec, &low);
-    return low && (((L.tc16_mask | L.fp32_mask | L.fp8_mask) >> *prec) & 1u);
+    return low && (((L.tc16_mask | L.fp32_mask | L.in16_mask) >> *prec) & 1u);
 }
 
 template <int D, int RP>
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kProjThreads, 1) proj_tc_kernel(const __grid_c
         for (int64_t bh = threadIdx.x; bh < L.B * L.H && !any; bh += blockDim.x) {
             int prec, low;
             get_decision(L.dec, bh, &prec, &low);
-            any = low && (((L.tc16_mask | L.fp32_mask | L.fp8_mask) >> prec) & 1u);
+            any = low && (((L.tc16_mask | L.fp32_mask | L.in16_mask) >> prec) & 1u);
         }
         if (!__syncthreads_or(any)) return;
     }
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kProjThreads, 1) proj_tc_kernel(const __grid_c
             for (int i = 0; i < RP; ++i) y[i] = i < rr ? round_to(y[i], in_dt) : 0.f;
             const bool to32 = (L.fp32_mask >> prec) & 1u;
             // E4M3 heads keep q_low/k_low in the inputs' dtype for the quantiser.
-            const bool f16 = ((L.fp8_mask >> prec) & 1u) ? (in_dt == ADA_F16) : ((L.f16_mask >> prec) & 1u);
+            const bool f16 = ((L.in16_mask >> prec) & 1u) ? (in_dt == ADA_F16) : ((L.f16_mask >> prec) & 1u);
             if constexpr (RP == 64) {
                 if (to32 ? L.tma32 : L.tma16) {
                     // Stage the 128-row tile in the swizzled box layout and let

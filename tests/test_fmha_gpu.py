@@ -107,6 +107,7 @@ LOW_CASES = [
     (torch.bfloat16, O.FP32, 64, 32, 300),     # V padded from 64 to 128 columns
     (torch.float16, O.FP32, 128, 17, 129),
     (torch.bfloat16, O.FP32, 128, 64, 1),
+    (torch.bfloat16, O.FP32, 96, 48, 150),     # SIMT projection: q_low/k_low scaled from fp32
 ]
 
 
