@@ -337,7 +337,7 @@ def main():
         }
         if allgather_ms is not None:
             line["allgather_outputs_ms"] = allgather_ms
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:  # the host-core baseline is an N=1 figure
             v_cpu, cores, desc = cpu_sample(w)
             line["cpu_baseline"] = {"value": v_cpu, "unit": "TFLOP/s", "cores": cores,
                                     "kind": "port", "sample": desc}
