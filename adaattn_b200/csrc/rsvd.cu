@@ -526,8 +526,9 @@ __device__ __forceinline__ void jacobi_rotation(double app, double aqq, double a
 }
 
 // Round structure: the rotations of all disjoint pairs are formed in
-// parallel (one thread each), then one warp per pair applies its rotation to
-// the two rows, and after a block barrier to the two columns of W and V.
+// parallel (one thread each), then every (pair, column) element of the two
+// rows is updated by its own thread, and after a block barrier every
+// (pair, row) element of the two columns of W and V.
 __global__ void __launch_bounds__(kEigThreads) eig_kernel(const double* Wall, int k, int r, float* s_out,
                                                           int64_t s_bs, int64_t s_st, double* mu_all,
                                                           double* mv_all, int max_sweeps) {
@@ -538,9 +539,7 @@ __global__ void __launch_bounds__(kEigThreads) eig_kernel(const double* Wall, in
     double* v = smd + kk * ld;  // [kk][ld]
     __shared__ double cs_c[kMaxSketch / 2], cs_s[kMaxSketch / 2];
     __shared__ double red[kEigThreads / 32];
-    __shared__ int rotations;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nwarps = blockDim.x >> 5;
+    __shared__ int2 pq[kMaxSketch / 2];
     const int b = blockIdx.x;
     const double* W = Wall + static_cast<int64_t>(b) * k * k;
     for (int idx = threadIdx.x; idx < kk * kk; idx += blockDim.x) {
@@ -567,8 +566,7 @@ __global__ void __launch_bounds__(kEigThreads) eig_kernel(const double* Wall, in
         // that a rotation only moves rounding noise around); a sweep without
         // any rotation ends the iteration.
         const double tiny = 1e-14 * sqrt(dg);
-        if (threadIdx.x == 0) rotations = 0;
-        __syncthreads();
+        int rotated = 0;
         for (int round = 0; round < kk - 1; ++round) {
             for (int pi = threadIdx.x; pi < half; pi += blockDim.x) {
                 int p, q;
@@ -578,45 +576,41 @@ __global__ void __launch_bounds__(kEigThreads) eig_kernel(const double* Wall, in
                 // |a_pq| > 1e-14 sqrt(|a_pp a_qq|), compared squared
                 if (fabs(apq) > tiny && apq * apq > 1e-28 * fabs(app * aqq)) {
                     jacobi_rotation(app, aqq, apq, &c, &s);
-                    if (s != 0.0) atomicAdd(&rotations, 1);
+                    rotated |= s != 0.0;
                 }
                 cs_c[pi] = c;
                 cs_s[pi] = s;
+                pq[pi] = make_int2(p, q);
             }
             __syncthreads();
-            for (int pi = warp; pi < half; pi += nwarps) {
+            for (int idx = threadIdx.x; idx < half * kk; idx += blockDim.x) {
+                const int pi = idx / kk, x = idx - pi * kk;
                 const double s = cs_s[pi];
                 if (s != 0.0) {
                     const double c = cs_c[pi];
-                    int p, q;
-                    rr_pair(kk, round, pi, &p, &q);
-                    for (int x = lane; x < kk; x += 32) {
-                        const double ap = a[p * ld + x], aq = a[q * ld + x];
-                        a[p * ld + x] = c * ap - s * aq;
-                        a[q * ld + x] = s * ap + c * aq;
-                    }
+                    const int p = pq[pi].x, q = pq[pi].y;
+                    const double ap = a[p * ld + x], aq = a[q * ld + x];
+                    a[p * ld + x] = c * ap - s * aq;
+                    a[q * ld + x] = s * ap + c * aq;
                 }
             }
             __syncthreads();
-            for (int pi = warp; pi < half; pi += nwarps) {
+            for (int idx = threadIdx.x; idx < half * kk; idx += blockDim.x) {
+                const int pi = idx / kk, x = idx - pi * kk;
                 const double s = cs_s[pi];
                 if (s == 0.0) continue;
                 const double c = cs_c[pi];
-                int p, q;
-                rr_pair(kk, round, pi, &p, &q);
-                for (int x = lane; x < kk; x += 32) {
-                    const double ap = a[x * ld + p], aq = a[x * ld + q];
-                    a[x * ld + p] = c * ap - s * aq;
-                    a[x * ld + q] = s * ap + c * aq;
-                    const double vp = v[x * ld + p], vq = v[x * ld + q];
-                    v[x * ld + p] = c * vp - s * vq;
-                    v[x * ld + q] = s * vp + c * vq;
-                }
+                const int p = pq[pi].x, q = pq[pi].y;
+                const double ap = a[x * ld + p], aq = a[x * ld + q];
+                a[x * ld + p] = c * ap - s * aq;
+                a[x * ld + q] = s * ap + c * aq;
+                const double vp = v[x * ld + p], vq = v[x * ld + q];
+                v[x * ld + p] = c * vp - s * vq;
+                v[x * ld + q] = s * vp + c * vq;
             }
             __syncthreads();
         }
-        if (rotations == 0) break;
-        __syncthreads();
+        if (!__syncthreads_or(rotated)) break;
     }
     for (int i = threadIdx.x; i < k; i += blockDim.x) {
         const double d = a[i * ld + i];
