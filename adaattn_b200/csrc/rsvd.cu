@@ -472,6 +472,7 @@ __global__ void __launch_bounds__(256) chol_inv_kernel(const double* Gall, int k
 // MV = MU / S (zero where S is zero). One CTA per matrix.
 // ---------------------------------------------------------------------------
 constexpr int kEigThreads = 1024;
+constexpr size_t kSvdSmemMax = 200 * 1024;
 
 __device__ double block_sum(double v, double* red) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -633,6 +634,126 @@ __global__ void __launch_bounds__(kEigThreads) eig_kernel(const double* Wall, in
             mu[c * r + rank] = v[c * ld + i];
             mv[c * r + rank] = v[c * ld + i] * inv;
         }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// One-sided (Hestenes) Jacobi SVD of B = Q^T A, k x n, in fp64: pairs of rows
+// are rotated until all rows are mutually orthogonal, so B = R diag(S) Z^T
+// with R the accumulated k x k rotation and the rows of Z unit vectors. One
+// half-warp per pair of each round-robin round (dot products, rotation, both
+// rows, both columns of R), one block barrier per round. Working on B
+// itself, not on B B^T, keeps the small singular values' relative accuracy.
+// Writes S (the r largest, descending), mu = R[:, those] (k x r; U = Q mu)
+// and Vh's rows (Z's rows; zero where S <= 1e-12 S_max, as for the Gram path).
+// ---------------------------------------------------------------------------
+constexpr int kSvdThreads = 1024;  // 64 half-warps >= kMaxSketch / 2 pairs
+
+size_t svdj_smem(int k, int64_t n) {
+    const int kk = k + (k & 1);
+    return (static_cast<size_t>(kk) * (n + 1) + static_cast<size_t>(kk) * (kk + 1)) * sizeof(double);
+}
+
+__global__ void __launch_bounds__(kSvdThreads) svdj_kernel(const float* zall, int64_t z_bs, int64_t z_ld, int k,
+                                                           int n, int r, float* s_out, int64_t s_bs, int64_t s_st,
+                                                           double* mu_all, float* vh, int64_t vh_bs, int64_t vh_rs,
+                                                           int64_t vh_cs, int max_sweeps) {
+    extern __shared__ double smd[];
+    const int kk = k + (k & 1);
+    const int ldb = n + 1, ldr = kk + 1;
+    double* bm = smd;              // [kk][ldb] rows of B, rotated in place
+    double* rm = smd + kk * ldb;   // [kk][ldr] R
+    __shared__ double sig[kMaxSketch + 1];
+    __shared__ int by_rank[kMaxSketch + 1];
+    const int b = blockIdx.x;
+    const float* z = zall + static_cast<int64_t>(b) * z_bs;
+    for (int idx = threadIdx.x; idx < kk * n; idx += kSvdThreads) {
+        const int i = idx / n, j = idx - i * n;
+        bm[i * ldb + j] = i < k ? static_cast<double>(z[i * z_ld + j]) : 0.0;
+    }
+    for (int idx = threadIdx.x; idx < kk * kk; idx += kSvdThreads) {
+        const int i = idx / kk, j = idx - i * kk;
+        rm[i * ldr + j] = i == j ? 1.0 : 0.0;
+    }
+    __syncthreads();
+    const int half = kk / 2;
+    const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
+    const unsigned hmask = (threadIdx.x & 16) ? 0xffff0000u : 0x0000ffffu;
+    for (int sweep = 0; sweep < max_sweeps; ++sweep) {
+        int rotated = 0;
+        for (int round = 0; round < kk - 1; ++round) {
+            if (hw < half) {
+                int p, q;
+                rr_pair(kk, round, hw, &p, &q);
+                double al = 0.0, be = 0.0, ga = 0.0;
+                for (int j = hl; j < n; j += 16) {
+                    const double x = bm[p * ldb + j], y = bm[q * ldb + j];
+                    al = fma(x, x, al);
+                    be = fma(y, y, be);
+                    ga = fma(x, y, ga);
+                }
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) {
+                    al += __shfl_xor_sync(hmask, al, o);
+                    be += __shfl_xor_sync(hmask, be, o);
+                    ga += __shfl_xor_sync(hmask, ga, o);
+                }
+                // rotate unless |b_p . b_q| <= 1e-15 |b_p| |b_q|
+                if (ga != 0.0 && ga * ga > 1e-30 * al * be) {
+                    double c, s;
+                    jacobi_rotation(al, be, ga, &c, &s);
+                    if (s != 0.0) {
+                        rotated = 1;
+                        for (int j = hl; j < n; j += 16) {
+                            const double x = bm[p * ldb + j], y = bm[q * ldb + j];
+                            bm[p * ldb + j] = c * x - s * y;
+                            bm[q * ldb + j] = s * x + c * y;
+                        }
+                        for (int i = hl; i < kk; i += 16) {
+                            const double x = rm[i * ldr + p], y = rm[i * ldr + q];
+                            rm[i * ldr + p] = c * x - s * y;
+                            rm[i * ldr + q] = s * x + c * y;
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+        }
+        if (!__syncthreads_or(rotated)) break;
+    }
+    // singular values: the row norms
+    for (int i = hw; i < k; i += kSvdThreads / 16) {
+        double a2 = 0.0;
+        for (int j = hl; j < n; j += 16) a2 = fma(bm[i * ldb + j], bm[i * ldb + j], a2);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) a2 += __shfl_xor_sync(hmask, a2, o);
+        if (hl == 0) sig[i] = sqrt(a2);
+    }
+    __syncthreads();
+    if (threadIdx.x < k) {
+        const int i = threadIdx.x;
+        const double d = sig[i];
+        int rank = 0;
+        for (int j = 0; j < k; ++j) {
+            const double e = sig[j];
+            if (e > d || (e == d && j < i)) ++rank;
+        }
+        if (rank < r) {
+            by_rank[rank] = i;
+            s_out[b * s_bs + rank * s_st] = static_cast<float>(d);
+            double* mu = mu_all + static_cast<int64_t>(b) * k * r;
+            for (int c = 0; c < k; ++c) mu[c * r + rank] = rm[c * ldr + i];
+        }
+    }
+    __syncthreads();
+    double smax = 0.0;
+    for (int j = 0; j < k; ++j) smax = fmax(smax, sig[j]);
+    for (int idx = threadIdx.x; idx < r * n; idx += kSvdThreads) {
+        const int rank = idx / n, j = idx - rank * n;
+        const int i = by_rank[rank];
+        const double sv = sig[i];
+        const double val = sv > 1e-12 * smax ? bm[i * ldb + j] / sv : 0.0;
+        vh[b * vh_bs + rank * vh_rs + j * vh_cs] = static_cast<float>(val);
     }
 }
 
@@ -967,6 +1088,7 @@ extern "C" int ada_rsvd(const AdaTensor* a, const AdaTensor* omega, int32_t rank
         (rc = allow_smem(gram64_kernel, static_cast<size_t>(P.k) * (kGramCols + 1) * 8)) ||
         (rc = allow_smem(chol_inv_kernel, static_cast<size_t>(2) * P.k * P.k * 8)) ||
         (rc = allow_smem(eig_kernel, static_cast<size_t>(2) * (P.k + 1) * (P.k + 2) * 8)) ||
+        (svdj_smem(P.k, P.n) <= kSvdSmemMax && (rc = allow_smem(svdj_kernel, svdj_smem(P.k, P.n)))) ||
         (rc = allow_smem(panel_apply_kernel<double>,
                          static_cast<size_t>(P.k) * ((P.k + 15) & ~15) * 8 + static_cast<size_t>(P.k) * 128 * 4)) ||
         (rc = allow_smem(panel_apply_kernel<float>,
@@ -1023,7 +1145,17 @@ extern "C" int ada_rsvd(const AdaTensor* a, const AdaTensor* omega, int32_t rank
         return rc;
     // B = Q^T A  (low_rank.py:96): the panel of (A^T Q)^T is B itself
     if ((rc = run_panel_gemm(C, 1, y, P.m, P.m4, z, P.n4))) return rc;
-    // B B^T = W diag(S^2) W^T
+    const size_t sv_smem = svdj_smem(P.k, P.n);
+    if (sv_smem <= kSvdSmemMax) {
+        // SVD of B by one-sided Jacobi; U = Q R[:, :r]  (low_rank.py:99-107)
+        svdj_kernel<<<static_cast<unsigned>(P.batch), kSvdThreads, sv_smem, strm>>>(
+            z, k * P.n4, P.n4, P.k, static_cast<int>(P.n), rank, static_cast<float*>(s->data), s->stride[0],
+            s->stride[1], mu, static_cast<float*>(vh->data), vh->stride[0], vh->stride[1], vh->stride[2], 30);
+        if (cudaGetLastError() != cudaSuccess) return fail_msg(ADA_ERR_LAUNCH, "Jacobi SVD launch failed");
+        return run_apply<float>(C, y, P.m, P.m4, mu, rank, 0, static_cast<float*>(u->data), u->stride[0],
+                                u->stride[2], u->stride[1]);
+    }
+    // Wide B: B B^T = W diag(S^2) W^T
     if ((rc = run_gram(C, z, P.n, P.n4, g))) return rc;
     const size_t eig_smem = static_cast<size_t>(2) * (P.k + (P.k & 1)) * (P.k + (P.k & 1) + 1) * 8;
     eig_kernel<<<static_cast<unsigned>(P.batch), kEigThreads, eig_smem, strm>>>(
