@@ -8,13 +8,14 @@ types; ``analyze`` / ``attention_forward`` for [B, H, N, D] tensors; and
 
 from .config import (AttentionConfig, AttentionError, KernelError, MemoryError,
                      NumericalError, PrecisionMode, ShapeError)
-from .core import DecisionTable, analyze, attention_forward
+from .core import DecisionTable, analyze, attention_forward, attention_forward_host
 from .attention import AdaAttention
 
 __all__ = [
     "AdaAttention", "AttentionConfig", "AttentionError", "KernelError", "MemoryError",
     "NumericalError", "PrecisionMode", "ShapeError", "DecisionTable", "analyze",
     "attention_forward",
+    "attention_forward_host",
 ]
 
 __version__ = "0.1.0"

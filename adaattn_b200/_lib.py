@@ -71,6 +71,9 @@ _SIGNATURES = {
                                                POINTER(AdaFwdParams), c_int32, c_int32]),
     "ada_attn_fwd": (c_int32, [_T, _T, _T, _T, _T, c_void_p, POINTER(AdaFwdParams),
                                c_int32, c_int32, _T, c_void_p, c_size_t, c_void_p]),
+    "ada_attn_fwd_host_buffer_bytes": (c_size_t, [_T, _T, _T, _T, POINTER(AdaFwdParams), c_int64]),
+    "ada_attn_fwd_host": (c_int32, [_T, _T, _T, _T, POINTER(AdaFwdParams), _T, c_int64, c_void_p,
+                                    c_size_t, c_void_p]),
     "ada_flash_attention_forward": (c_int32, [_T, _T, _T, c_float, c_int32, _T, c_void_p]),
     "ada_compute_entropy": (c_int32, [_T, c_void_p, c_void_p]),
     "ada_estimate_effective_rank": (c_int32, [_T, c_void_p, c_void_p]),

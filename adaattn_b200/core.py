@@ -190,5 +190,71 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scal
     return out
 
 
+def _host_params(scale, causal, static_precision, static_low_rank, fp8_mode):
+    p = _lib.AdaFwdParams()
+    p.scale = float(scale)
+    p.causal = int(bool(causal))
+    p.fp8_mode = 0 if fp8_mode == "e4m3" else 1
+    p.static_precision = PrecisionMode.coerce(static_precision).code
+    p.static_low_rank = int(bool(static_low_rank))
+    return p
+
+
+def host_buffer_bytes(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float,
+                      static_precision: PrecisionMode = PrecisionMode.FP16,
+                      static_low_rank: bool = False, w_down: Optional[torch.Tensor] = None,
+                      chunk_rows: int = 0) -> int:
+    """Device staging bytes `attention_forward_host` needs for these host operands."""
+    lib = _lib.load()
+    p = _host_params(scale, False, static_precision, static_low_rank, "e4m3")
+    tw = _lib.tensor(w_down.detach().contiguous()) if w_down is not None else None
+    need = int(lib.ada_attn_fwd_host_buffer_bytes(_lib.tensor(q), _lib.tensor(k), _lib.tensor(v), tw, p,
+                                                  int(chunk_rows)))
+    if need == 0:
+        raise ShapeError(f"ada_attn_fwd_host_buffer_bytes: {_lib.last_error()}")
+    return need
+
+
+def attention_forward_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float,
+                           causal: bool = False,
+                           static_precision: PrecisionMode = PrecisionMode.FP16,
+                           static_low_rank: bool = False, w_down: Optional[torch.Tensor] = None,
+                           fp8_mode: str = "e4m3", out: Optional[torch.Tensor] = None,
+                           device: Optional[torch.device] = None, chunk_rows: int = 0,
+                           buffer: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """`attention_forward` for host-resident [B, H, N, D] operands (contiguous;
+    pinned memory lets the copies overlap): batch-row chunks are copied in,
+    computed and copied out on overlapping streams (``ada_attn_fwd_host``).
+    Every slice takes ``static_precision`` / ``static_low_rank``. Returns the
+    host ``out`` (allocated pinned when not given); it is complete once the
+    current stream of ``device`` is. ``buffer``: an optional device uint8
+    tensor reused as the staging buffer."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if dev.type != "cuda":
+        raise TypeError("device must be a CUDA device")
+    for t in (q, k, v):
+        if t.is_cuda:
+            raise TypeError("attention_forward_host takes host tensors; use attention_forward")
+        if not t.is_contiguous():
+            raise ShapeError("host operands must be contiguous [B, H, N, D]")
+    lib = _lib.load()
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    p = _host_params(scale, causal, static_precision, static_low_rank, fp8_mode)
+    w_keep = w_down.detach().to(dev).contiguous() if w_down is not None else None
+    tw = _lib.tensor(w_keep) if w_keep is not None else None
+    tq, tk, tv, to = (_lib.tensor(t) for t in (q, k, v, out))
+    need = int(lib.ada_attn_fwd_host_buffer_bytes(tq, tk, tv, tw, p, int(chunk_rows)))
+    if need == 0:
+        raise ShapeError(f"ada_attn_fwd_host_buffer_bytes: {_lib.last_error()}")
+    if buffer is None or buffer.numel() < need or buffer.device != dev:
+        buffer = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.ada_attn_fwd_host(tq, tk, tv, tw, p, to, int(chunk_rows), buffer.data_ptr(),
+                                   buffer.numel(), _lib.stream_ptr(dev))
+    _lib.check(rc, "ada_attn_fwd_host")
+    return out
+
+
 def default_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)

@@ -451,6 +451,91 @@ int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) { return encoder(f
 uint64_t default_wait_timeout_ns() { return wait_timeout_ns(); }
 }  // namespace ada
 
+namespace ada {
+namespace {
+// ---------------------------------------------------------------------------
+// Host-resident operands: batch-row chunks streamed through a device staging
+// buffer on three streams per device (copy in, forward, copy out), so the
+// PCIe transfers in both directions overlap each other and the kernels.
+// ---------------------------------------------------------------------------
+struct HostPipe {
+    cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
+    cudaEvent_t start = nullptr, in[2] = {nullptr, nullptr}, comp[2] = {nullptr, nullptr},
+                out[2] = {nullptr, nullptr};
+};
+HostPipe g_pipe[kMaxDevices];
+
+int host_pipe(int dev, HostPipe** hp) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    HostPipe& p = g_pipe[dev];
+    if (p.s_in == nullptr) {
+        bool ok = cudaStreamCreateWithFlags(&p.s_in, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&p.s_comp, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&p.s_out, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming) == cudaSuccess;
+        for (int i = 0; ok && i < 2; ++i)
+            ok = cudaEventCreateWithFlags(&p.in[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&p.comp[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&p.out[i], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            p = HostPipe{};
+            return fail(ADA_ERR_CUDA, "creating the host-pipeline streams failed");
+        }
+    }
+    *hp = &p;
+    return ADA_OK;
+}
+
+// Row geometry of a host operand: [B, H, N, D] with every batch row one
+// contiguous block; returns its bytes per batch row, or 0.
+int64_t host_row_bytes(const AdaTensor* t) {
+    if (t == nullptr || t->data == nullptr || t->ndim != 4) return 0;
+    const int64_t eb = elt_bytes(t->dtype);
+    if (eb == 0 || t->stride[3] != 1 || t->stride[2] != t->shape[3] || t->stride[1] != t->shape[2] * t->shape[3])
+        return 0;
+    if (t->shape[0] > 1 && t->stride[0] != t->shape[1] * t->shape[2] * t->shape[3]) return 0;
+    return t->shape[1] * t->shape[2] * t->shape[3] * eb;
+}
+
+int64_t host_chunk_rows(const AdaTensor* q, int64_t chunk_rows) {
+    if (chunk_rows > 0) return chunk_rows < q->shape[0] ? chunk_rows : q->shape[0];
+    // about 32 MB of q per chunk, at least 4 chunks when the batch allows
+    const int64_t rb = host_row_bytes(q);
+    int64_t c = rb > 0 ? (int64_t{32} << 20) / rb : 1;
+    if (c < 1) c = 1;
+    const int64_t quarter = (q->shape[0] + 3) / 4;
+    if (c > quarter) c = quarter;
+    return c < 1 ? 1 : c;
+}
+
+AdaTensor chunk_view(const AdaTensor* t, void* base, int64_t rows) {
+    AdaTensor c = *t;
+    c.data = base;
+    c.shape[0] = rows;
+    c.stride[0] = t->shape[1] * t->shape[2] * t->shape[3];
+    return c;
+}
+
+int host_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const AdaTensor* w_down,
+              const AdaFwdParams* params, int64_t rows, size_t* ws_bytes, size_t* total) {
+    const int64_t rq = host_row_bytes(q), rk = host_row_bytes(k), rv = host_row_bytes(v);
+    if (rq == 0 || rk == 0 || rv == 0)
+        return fail(ADA_ERR_LAYOUT, "host operands must be [B,H,N,D] with contiguous batch rows");
+    AdaTensor cq = chunk_view(q, q->data, rows), ck = chunk_view(k, k->data, rows), cv = chunk_view(v, v->data, rows);
+    Plan P;
+    int rc = build_plan(&cq, &ck, &cv, w_down, nullptr, params, 0, params->static_low_rank, &P);
+    if (rc) return rc;
+    *ws_bytes = P.total;
+    // two slots of q, k, v, out (out has q's geometry) + one forward workspace
+    const size_t slot = align256(static_cast<size_t>(rq * rows)) * 2 + align256(static_cast<size_t>(rk * rows)) +
+                        align256(static_cast<size_t>(rv * rows));
+    *total = 2 * slot + align256(P.total);
+    return ADA_OK;
+}
+
+}  // namespace
+}  // namespace ada
+
 using namespace ada;
 
 extern "C" {
@@ -955,6 +1040,95 @@ int ada_determine_target_ranks(const float* eff, int64_t n, int64_t min_rank, in
     if ((eff == nullptr || ranks_out == nullptr) && n > 0) return fail(ADA_ERR_INVALID, "null argument");
     rc = launch_target_ranks(eff, n, min_rank, max_rank, threshold, ranks_out, static_cast<cudaStream_t>(stream));
     return rc ? fail(rc, "target-rank launch failed") : ADA_OK;
+}
+
+size_t ada_attn_fwd_host_buffer_bytes(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v,
+                                      const AdaTensor* w_down, const AdaFwdParams* params, int64_t chunk_rows) {
+    if (q == nullptr || k == nullptr || v == nullptr || params == nullptr || q->ndim != 4) return 0;
+    size_t ws = 0, total = 0;
+    if (host_plan(q, k, v, w_down, params, host_chunk_rows(q, chunk_rows), &ws, &total)) return 0;
+    return total;
+}
+
+int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const AdaTensor* w_down,
+                      const AdaFwdParams* params, AdaTensor* out, int64_t chunk_rows, void* device_buffer,
+                      size_t buffer_bytes, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    int dev;
+    if ((rc = current_device(&dev))) return rc;
+    if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || params == nullptr)
+        return fail(ADA_ERR_INVALID, "null argument");
+    if (q->ndim != 4 || k->ndim != 4 || v->ndim != 4 || out->ndim != 4)
+        return fail(ADA_ERR_SHAPE, "host operands are [B,H,N,D]");
+    const int64_t B = q->shape[0];
+    if (k->shape[0] != B || v->shape[0] != B || out->shape[0] != B)
+        return fail(ADA_ERR_SHAPE, "batch extents differ");
+    const int64_t ro = host_row_bytes(out);
+    if (ro == 0 || ro != host_row_bytes(q) || out->dtype != q->dtype)
+        return fail(ADA_ERR_LAYOUT, "out must be a host [B,H,Nq,D] buffer shaped like q");
+    const int64_t rows = host_chunk_rows(q, chunk_rows);
+    size_t ws_bytes = 0, total = 0;
+    if ((rc = host_plan(q, k, v, w_down, params, rows, &ws_bytes, &total))) return rc;
+    if (device_buffer == nullptr || buffer_bytes < total)
+        return fail(ADA_ERR_WORKSPACE, "device buffer needs %zu bytes, got %zu", total, buffer_bytes);
+    if (B == 0) return ADA_OK;
+    HostPipe* hp;
+    if ((rc = host_pipe(dev, &hp))) return rc;
+    const int64_t rq = host_row_bytes(q), rk = host_row_bytes(k), rv = host_row_bytes(v);
+    uint8_t* base = static_cast<uint8_t*>(device_buffer);
+    const size_t sq = align256(static_cast<size_t>(rq * rows)), sk = align256(static_cast<size_t>(rk * rows)),
+                 sv = align256(static_cast<size_t>(rv * rows));
+    const size_t slot = 2 * sq + sk + sv;
+    void* ws = base + 2 * slot;
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    auto ck = [&](cudaError_t e, const char* what) {
+        return e == cudaSuccess ? ADA_OK : fail(ADA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    };
+    if ((rc = ck(cudaEventRecord(hp->start, caller), "event record")) ||
+        (rc = ck(cudaStreamWaitEvent(hp->s_in, hp->start, 0), "stream wait")) ||
+        (rc = ck(cudaStreamWaitEvent(hp->s_comp, hp->start, 0), "stream wait")) ||
+        (rc = ck(cudaStreamWaitEvent(hp->s_out, hp->start, 0), "stream wait")))
+        return rc;
+    const int64_t nchunks = (B + rows - 1) / rows;
+    int last = 0;
+    for (int64_t c = 0; c < nchunks; ++c) {
+        const int sl = static_cast<int>(c & 1);
+        const int64_t r0 = c * rows, n = (B - r0) < rows ? (B - r0) : rows;
+        uint8_t* dq = base + sl * slot;
+        uint8_t* dk = dq + sq;
+        uint8_t* dv = dk + sk;
+        uint8_t* dout = dv + sv;
+        // copy in once the forward two chunks back has read this slot
+        if (c >= 2 && (rc = ck(cudaStreamWaitEvent(hp->s_in, hp->comp[sl], 0), "stream wait"))) return rc;
+        if ((rc = ck(cudaMemcpyAsync(dq, static_cast<const uint8_t*>(q->data) + r0 * rq, n * rq,
+                                     cudaMemcpyHostToDevice, hp->s_in), "copy of q")) ||
+            (rc = ck(cudaMemcpyAsync(dk, static_cast<const uint8_t*>(k->data) + r0 * rk, n * rk,
+                                     cudaMemcpyHostToDevice, hp->s_in), "copy of k")) ||
+            (rc = ck(cudaMemcpyAsync(dv, static_cast<const uint8_t*>(v->data) + r0 * rv, n * rv,
+                                     cudaMemcpyHostToDevice, hp->s_in), "copy of v")) ||
+            (rc = ck(cudaEventRecord(hp->in[sl], hp->s_in), "event record")))
+            return rc;
+        // forward once the inputs landed and the copy out two chunks back has read the output slot
+        if ((rc = ck(cudaStreamWaitEvent(hp->s_comp, hp->in[sl], 0), "stream wait"))) return rc;
+        if (c >= 2 && (rc = ck(cudaStreamWaitEvent(hp->s_comp, hp->out[sl], 0), "stream wait"))) return rc;
+        AdaTensor cq = chunk_view(q, dq, n), ckt = chunk_view(k, dk, n), cv = chunk_view(v, dv, n),
+                  co = chunk_view(out, dout, n);
+        if ((rc = ada_attn_fwd(&cq, &ckt, &cv, w_down, nullptr, nullptr, params, 0, params->static_low_rank, &co,
+                               ws, ws_bytes, hp->s_comp)))
+            return rc;
+        if ((rc = ck(cudaEventRecord(hp->comp[sl], hp->s_comp), "event record"))) return rc;
+        // copy out
+        if ((rc = ck(cudaStreamWaitEvent(hp->s_out, hp->comp[sl], 0), "stream wait")) ||
+            (rc = ck(cudaMemcpyAsync(static_cast<uint8_t*>(out->data) + r0 * ro, dout, n * ro,
+                                     cudaMemcpyDeviceToHost, hp->s_out), "copy of out")) ||
+            (rc = ck(cudaEventRecord(hp->out[sl], hp->s_out), "event record")))
+            return rc;
+        last = sl;
+    }
+    // the caller's stream continues after the last copy out (copies out run in order)
+    return ck(cudaStreamWaitEvent(caller, hp->out[last], 0), "stream wait");
 }
 
 int ada_debug_bounded_wait(uint64_t timeout_ns, void* stream) {

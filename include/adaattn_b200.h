@@ -172,6 +172,25 @@ int         ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor
                          AdaTensor* out, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* ada_attn_fwd for host-resident operands (no counterpart in the reference;
+ * the reference's callers pass host tensors and let PyTorch copy them). q, k,
+ * v and out point to host memory (pinned for the copies to overlap), each a
+ * [B,H,N,D] tensor whose batch rows are contiguous blocks. Batch-row chunks
+ * (chunk_rows, or about 32 MB of q per chunk when 0) stream through
+ * `device_buffer` (sized by ada_attn_fwd_host_buffer_bytes): copies in, the
+ * forward and copies out run on three internal streams, both PCIe
+ * directions overlapping each other and the kernels. Every head takes
+ * params->static_precision / static_low_rank (w_down on the device when
+ * low rank); no mask. Ordered after prior work on `stream`, which waits for
+ * the last copy out: `out` is complete once `stream` is. */
+size_t      ada_attn_fwd_host_buffer_bytes(const AdaTensor* q, const AdaTensor* k,
+                                           const AdaTensor* v, const AdaTensor* w_down,
+                                           const AdaFwdParams* params, int64_t chunk_rows);
+int         ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v,
+                              const AdaTensor* w_down, const AdaFwdParams* params,
+                              AdaTensor* out, int64_t chunk_rows, void* device_buffer,
+                              size_t buffer_bytes, void* stream);
+
 /* _adaattn_cuda.flash_attention_forward (bindings.cpp:21-68): q, k, v, out are
  * [B, N, H, D] fp16/bf16 (or f32); scale <= 0 means 1/sqrt(D). */
 int         ada_flash_attention_forward(const AdaTensor* q, const AdaTensor* k,

@@ -70,3 +70,11 @@ def test_workspace_query_is_host_only():
     p.static_precision = 3  # FP8 E4M3: 8-bit copies plus scales
     n8 = lib.ada_attn_fwd_workspace_bytes(t, t, t, None, None, p, 0, 0)
     assert n8 >= 3 * 2 * 4 * 256 * 128
+
+
+def test_host_pipeline_checks_layout_before_any_device_work():
+    import torch
+    from adaattn_b200 import ShapeError, attention_forward_host
+    q = torch.zeros(2, 4, 8, 16, dtype=torch.float16)
+    with pytest.raises(ShapeError):
+        attention_forward_host(q.transpose(1, 2), q, q, scale=0.25, device="cuda:0")
