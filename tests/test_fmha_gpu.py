@@ -74,6 +74,8 @@ DENSE_CASES = [
     (torch.float16, O.FP32, 64, 200, 77),
     (torch.bfloat16, O.FP32, 96, 100, 100),    # head dim padded to 128
     (torch.bfloat16, O.FP32, 128, 1, 1),
+    (torch.bfloat16, O.FP32, 32, 130, 70),     # head dim 32: scaled fp16 q/k, Nq != Nk
+    (torch.float16, O.FP32, 128, 64, 333),     # Nq < Nk, fp16 q/k read in place
 ]
 
 
@@ -252,3 +254,19 @@ def test_fp32_low_rank_tensor_core_masks(cuda_device):
         m = max(1.0, ref[ok].abs().max().item())
         err = (out[ok].float() - ref[ok].float()).abs().max().item()
         assert err <= 1e-5 * m + 2.0 ** -8 * m, f"mask {mask.dtype}: err {err:.3e}"
+
+
+@pytest.mark.parametrize("low", [False, True])
+def test_fp32_tensor_core_strided_views_and_masks(low, cuda_device):
+    """FP32 heads of bf16 [B, N, H, D] views (the module's layout) with a
+    float mask and causal masking, dense and low rank."""
+    b, n, h, d = 2, 190, 3, 128
+    g = torch.Generator().manual_seed(41)
+    x = (torch.randn(3, b, n, h, d, generator=g) * 3.0).to(torch.bfloat16)
+    q, k, v = (x[i].transpose(1, 2) for i in range(3))
+    w = _w_down(d, 64, torch.bfloat16) if low else None
+    add = torch.randn(b, 1, n, n, generator=g)
+    out, scale = _run(q, k, v, O.FP32, low, True, cuda_device, mask=add, w=w)
+    for hh in range(h):
+        check_head(out[:, hh:hh + 1], q[:, hh:hh + 1], k[:, hh:hh + 1], v[:, hh:hh + 1], O.FP32, low,
+                   scale, True, mask=add, w_down=w, label=f"h{hh}")
