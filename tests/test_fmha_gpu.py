@@ -270,3 +270,31 @@ def test_fp32_tensor_core_strided_views_and_masks(low, cuda_device):
     for hh in range(h):
         check_head(out[:, hh:hh + 1], q[:, hh:hh + 1], k[:, hh:hh + 1], v[:, hh:hh + 1], O.FP32, low,
                    scale, True, mask=add, w_down=w, label=f"h{hh}")
+
+
+@pytest.mark.parametrize("prec", [O.BF16, O.FP16, O.FP32])
+def test_long_sequence_rows_against_torch_fp32(prec, cuda_device):
+    """N = 32768: row blocks at the start, the middle and the end of the
+    sequence against a float32 torch evaluation of the same rows on the GPU
+    (the CPU oracle would take minutes at this length)."""
+    b, h, n, d = 1, 2, 32768, 128
+    g = torch.Generator(device=cuda_device).manual_seed(51)
+    q, k, v = (torch.randn(b, h, n, d, device=cuda_device, generator=g).bfloat16() for _ in range(3))
+    scale = 1.0 / math.sqrt(d)
+    for causal in (False, True):
+        out = attention_forward(q, k, v, scale=scale, causal=causal, static_precision=PM[prec])
+        torch.cuda.synchronize()
+        for r0 in (0, n // 2 - 64, n - 128):
+            rows = slice(r0, r0 + 128)
+            s = (q[:, :, rows].float() @ k.float().transpose(-1, -2)) * scale
+            if causal:
+                qi = torch.arange(r0, r0 + 128, device=cuda_device)[:, None]
+                kj = torch.arange(n, device=cuda_device)[None, :]
+                s = s.masked_fill(kj > qi, float("-inf"))
+            ref = torch.softmax(s, -1) @ v.float()
+            err = (out[:, :, rows].float() - ref).abs().max().item()
+            m = max(1.0, ref.abs().max().item())
+            # bf16 outputs: one unit in the last place (2^-8 relative); FP32 heads
+            # otherwise 1e-5, 16-bit P 2e-3 more
+            bar = (2 ** -8 + 1e-5) * m if prec == O.FP32 else (2 ** -7 + 2e-3) * m
+            assert err <= bar, f"prec {prec} causal {causal} rows {r0}: err {err:.3e}"
