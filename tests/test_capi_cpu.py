@@ -78,3 +78,27 @@ def test_host_pipeline_checks_layout_before_any_device_work():
     q = torch.zeros(2, 4, 8, 16, dtype=torch.float16)
     with pytest.raises(ShapeError):
         attention_forward_host(q.transpose(1, 2), q, q, scale=0.25, device="cuda:0")
+
+
+def test_workspace_queries_without_a_gpu():
+    """Plan-only queries need no device: the forward workspace grows with the
+    FP32 tensor-core operands when FP32 heads of 16-bit inputs are possible,
+    and the host pipeline's staging buffer holds two chunks plus a workspace."""
+    import torch
+    lib = _lib.load()
+    q = torch.zeros(4, 2, 256, 128, dtype=torch.bfloat16)
+    tq = _lib.tensor(q)
+    p = _lib.AdaFwdParams()
+    p.scale = 0.125
+    p.static_precision = 2  # BF16
+    dense_bf16 = lib.ada_attn_fwd_workspace_bytes(tq, tq, tq, None, None, p, 0, 0)
+    p.static_precision = 0  # FP32: dense heads read q, k in place; v goes to a scaled fp16 copy
+    dense_fp32 = lib.ada_attn_fwd_workspace_bytes(tq, tq, tq, None, None, p, 0, 0)
+    assert dense_fp32 >= dense_bf16 + 4 * 2 * 256 * 128 * 2
+    p.static_precision = 2
+    one = lib.ada_attn_fwd_host_buffer_bytes(tq, tq, tq, None, p, 1)
+    two = lib.ada_attn_fwd_host_buffer_bytes(tq, tq, tq, None, p, 2)
+    row = 2 * 256 * 128 * 2
+    assert one >= 2 * 4 * row and two >= 2 * 4 * 2 * row and two > one
+    bad = _lib.tensor(q.transpose(2, 3))
+    assert lib.ada_attn_fwd_host_buffer_bytes(bad, tq, tq, None, p, 1) == 0
