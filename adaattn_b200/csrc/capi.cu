@@ -459,6 +459,7 @@ namespace {
 // PCIe transfers in both directions overlap each other and the kernels.
 // ---------------------------------------------------------------------------
 struct HostPipe {
+    std::mutex mu;  // one call's enqueue sequence at a time (the streams and events are shared)
     cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
     cudaEvent_t start = nullptr, in[2] = {nullptr, nullptr}, comp[2] = {nullptr, nullptr},
                 out[2] = {nullptr, nullptr};
@@ -478,7 +479,7 @@ int host_pipe(int dev, HostPipe** hp) {
                  cudaEventCreateWithFlags(&p.comp[i], cudaEventDisableTiming) == cudaSuccess &&
                  cudaEventCreateWithFlags(&p.out[i], cudaEventDisableTiming) == cudaSuccess;
         if (!ok) {
-            p = HostPipe{};
+            p.s_in = p.s_comp = p.s_out = nullptr;
             return fail(ADA_ERR_CUDA, "creating the host-pipeline streams failed");
         }
     }
@@ -1076,6 +1077,7 @@ int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v
     if (B == 0) return ADA_OK;
     HostPipe* hp;
     if ((rc = host_pipe(dev, &hp))) return rc;
+    std::lock_guard<std::mutex> pipe_lock(hp->mu);
     const int64_t rq = host_row_bytes(q), rk = host_row_bytes(k), rv = host_row_bytes(v);
     uint8_t* base = static_cast<uint8_t*>(device_buffer);
     const size_t sq = align256(static_cast<size_t>(rq * rows)), sk = align256(static_cast<size_t>(rk * rows)),

@@ -182,7 +182,8 @@ int         ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor
  * directions overlapping each other and the kernels. Every head takes
  * params->static_precision / static_low_rank (w_down on the device when
  * low rank); no mask. Ordered after prior work on `stream`, which waits for
- * the last copy out: `out` is complete once `stream` is. */
+ * the last copy out: `out` is complete once `stream` is. Concurrent calls on
+ * one device queue one after another on the shared internal streams. */
 size_t      ada_attn_fwd_host_buffer_bytes(const AdaTensor* q, const AdaTensor* k,
                                            const AdaTensor* v, const AdaTensor* w_down,
                                            const AdaFwdParams* params, int64_t chunk_rows);
