@@ -931,7 +931,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         }
         if ((rc = launch_fmha_tc(L, s))) return fail(rc, "fp32 tensor-core attention launch failed");
     }
-    // ---- fp32 heads on the CUDA cores ---------------------------------------
+    // ---- remaining FP32 heads (fp32 inputs, ranks above 64) on the CUDA cores ----
     if (P.possible & P.fp32_mask) {
         for (int low = 0; low < 2; ++low) {
             if (low ? (!P.low_possible || P.split_low) : (!P.dense_possible || P.split_dense)) continue;
