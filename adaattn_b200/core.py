@@ -203,13 +203,13 @@ def _host_params(scale, causal, static_precision, static_low_rank, fp8_mode):
 def host_buffer_bytes(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float,
                       static_precision: PrecisionMode = PrecisionMode.FP16,
                       static_low_rank: bool = False, w_down: Optional[torch.Tensor] = None,
-                      chunk_rows: int = 0) -> int:
+                      chunk_slices: int = 0) -> int:
     """Device staging bytes `attention_forward_host` needs for these host operands."""
     lib = _lib.load()
     p = _host_params(scale, False, static_precision, static_low_rank, "e4m3")
     tw = _lib.tensor(w_down.detach().contiguous()) if w_down is not None else None
     need = int(lib.ada_attn_fwd_host_buffer_bytes(_lib.tensor(q), _lib.tensor(k), _lib.tensor(v), tw, p,
-                                                  int(chunk_rows)))
+                                                  int(chunk_slices)))
     if need == 0:
         raise ShapeError(f"ada_attn_fwd_host_buffer_bytes: {_lib.last_error()}")
     return need
@@ -220,10 +220,10 @@ def attention_forward_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                            static_precision: PrecisionMode = PrecisionMode.FP16,
                            static_low_rank: bool = False, w_down: Optional[torch.Tensor] = None,
                            fp8_mode: str = "e4m3", out: Optional[torch.Tensor] = None,
-                           device: Optional[torch.device] = None, chunk_rows: int = 0,
+                           device: Optional[torch.device] = None, chunk_slices: int = 0,
                            buffer: Optional[torch.Tensor] = None) -> torch.Tensor:
     """`attention_forward` for host-resident [B, H, N, D] operands (contiguous;
-    pinned memory lets the copies overlap): batch-row chunks are copied in,
+    pinned memory lets the copies overlap): chunks of (b, h) slices are copied in,
     computed and copied out on overlapping streams (``ada_attn_fwd_host``).
     Every slice takes ``static_precision`` / ``static_low_rank``. Returns the
     host ``out`` (allocated pinned when not given); it is complete once the
@@ -244,13 +244,13 @@ def attention_forward_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     w_keep = w_down.detach().to(dev).contiguous() if w_down is not None else None
     tw = _lib.tensor(w_keep) if w_keep is not None else None
     tq, tk, tv, to = (_lib.tensor(t) for t in (q, k, v, out))
-    need = int(lib.ada_attn_fwd_host_buffer_bytes(tq, tk, tv, tw, p, int(chunk_rows)))
+    need = int(lib.ada_attn_fwd_host_buffer_bytes(tq, tk, tv, tw, p, int(chunk_slices)))
     if need == 0:
         raise ShapeError(f"ada_attn_fwd_host_buffer_bytes: {_lib.last_error()}")
     if buffer is None or buffer.numel() < need or buffer.device != dev:
         buffer = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        rc = lib.ada_attn_fwd_host(tq, tk, tv, tw, p, to, int(chunk_rows), buffer.data_ptr(),
+        rc = lib.ada_attn_fwd_host(tq, tk, tv, tw, p, to, int(chunk_slices), buffer.data_ptr(),
                                    buffer.numel(), _lib.stream_ptr(dev))
     _lib.check(rc, "ada_attn_fwd_host")
     return out

@@ -487,41 +487,46 @@ int host_pipe(int dev, HostPipe** hp) {
     return ADA_OK;
 }
 
-// Row geometry of a host operand: [B, H, N, D] with every batch row one
-// contiguous block; returns its bytes per batch row, or 0.
-int64_t host_row_bytes(const AdaTensor* t) {
+// Slice geometry of a host operand: a contiguous [B, H, N, D] tensor, so every
+// (b, h) slice is one block and consecutive slices are adjacent; returns the
+// bytes per slice, or 0.
+int64_t host_slice_bytes(const AdaTensor* t) {
     if (t == nullptr || t->data == nullptr || t->ndim != 4) return 0;
     const int64_t eb = elt_bytes(t->dtype);
-    if (eb == 0 || t->stride[3] != 1 || t->stride[2] != t->shape[3] || t->stride[1] != t->shape[2] * t->shape[3])
-        return 0;
+    if (eb == 0 || t->stride[3] != 1 || t->stride[2] != t->shape[3]) return 0;
+    if (t->shape[1] > 1 && t->stride[1] != t->shape[2] * t->shape[3]) return 0;
     if (t->shape[0] > 1 && t->stride[0] != t->shape[1] * t->shape[2] * t->shape[3]) return 0;
-    return t->shape[1] * t->shape[2] * t->shape[3] * eb;
+    return t->shape[2] * t->shape[3] * eb;
 }
 
-int64_t host_chunk_rows(const AdaTensor* q, int64_t chunk_rows) {
-    if (chunk_rows > 0) return chunk_rows < q->shape[0] ? chunk_rows : q->shape[0];
-    // about 32 MB of q per chunk, at least 4 chunks when the batch allows
-    const int64_t rb = host_row_bytes(q);
-    int64_t c = rb > 0 ? (int64_t{32} << 20) / rb : 1;
-    if (c < 1) c = 1;
-    const int64_t quarter = (q->shape[0] + 3) / 4;
+int64_t host_chunk_slices(const AdaTensor* q, int64_t chunk_slices) {
+    const int64_t S = q->shape[0] * q->shape[1];
+    if (chunk_slices > 0) return chunk_slices < S ? chunk_slices : S;
+    // about 16 MB of q per chunk, at least 4 chunks when there are enough slices
+    const int64_t sb = host_slice_bytes(q);
+    int64_t c = sb > 0 ? (int64_t{16} << 20) / sb : 1;
+    const int64_t quarter = (S + 3) / 4;
     if (c > quarter) c = quarter;
     return c < 1 ? 1 : c;
 }
 
-AdaTensor chunk_view(const AdaTensor* t, void* base, int64_t rows) {
+// n consecutive slices as one [1, n, N, D] tensor (every slice takes the
+// static decision, so which batch row a slice came from does not matter).
+AdaTensor chunk_view(const AdaTensor* t, void* base, int64_t n) {
     AdaTensor c = *t;
     c.data = base;
-    c.shape[0] = rows;
-    c.stride[0] = t->shape[1] * t->shape[2] * t->shape[3];
+    c.shape[0] = 1;
+    c.shape[1] = n;
+    c.stride[1] = t->shape[2] * t->shape[3];
+    c.stride[0] = n * c.stride[1];
     return c;
 }
 
 int host_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const AdaTensor* w_down,
               const AdaFwdParams* params, int64_t rows, size_t* ws_bytes, size_t* total) {
-    const int64_t rq = host_row_bytes(q), rk = host_row_bytes(k), rv = host_row_bytes(v);
+    const int64_t rq = host_slice_bytes(q), rk = host_slice_bytes(k), rv = host_slice_bytes(v);
     if (rq == 0 || rk == 0 || rv == 0)
-        return fail(ADA_ERR_LAYOUT, "host operands must be [B,H,N,D] with contiguous batch rows");
+        return fail(ADA_ERR_LAYOUT, "host operands must be contiguous [B,H,N,D] tensors");
     AdaTensor cq = chunk_view(q, q->data, rows), ck = chunk_view(k, k->data, rows), cv = chunk_view(v, v->data, rows);
     Plan P;
     int rc = build_plan(&cq, &ck, &cv, w_down, nullptr, params, 0, params->static_low_rank, &P);
@@ -1044,15 +1049,15 @@ int ada_determine_target_ranks(const float* eff, int64_t n, int64_t min_rank, in
 }
 
 size_t ada_attn_fwd_host_buffer_bytes(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v,
-                                      const AdaTensor* w_down, const AdaFwdParams* params, int64_t chunk_rows) {
+                                      const AdaTensor* w_down, const AdaFwdParams* params, int64_t chunk_slices) {
     if (q == nullptr || k == nullptr || v == nullptr || params == nullptr || q->ndim != 4) return 0;
     size_t ws = 0, total = 0;
-    if (host_plan(q, k, v, w_down, params, host_chunk_rows(q, chunk_rows), &ws, &total)) return 0;
+    if (host_plan(q, k, v, w_down, params, host_chunk_slices(q, chunk_slices), &ws, &total)) return 0;
     return total;
 }
 
 int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const AdaTensor* w_down,
-                      const AdaFwdParams* params, AdaTensor* out, int64_t chunk_rows, void* device_buffer,
+                      const AdaFwdParams* params, AdaTensor* out, int64_t chunk_slices, void* device_buffer,
                       size_t buffer_bytes, void* stream) {
     unsigned int* st;
     int rc = device_setup(&st);
@@ -1063,13 +1068,15 @@ int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v
         return fail(ADA_ERR_INVALID, "null argument");
     if (q->ndim != 4 || k->ndim != 4 || v->ndim != 4 || out->ndim != 4)
         return fail(ADA_ERR_SHAPE, "host operands are [B,H,N,D]");
-    const int64_t B = q->shape[0];
-    if (k->shape[0] != B || v->shape[0] != B || out->shape[0] != B)
-        return fail(ADA_ERR_SHAPE, "batch extents differ");
-    const int64_t ro = host_row_bytes(out);
-    if (ro == 0 || ro != host_row_bytes(q) || out->dtype != q->dtype)
-        return fail(ADA_ERR_LAYOUT, "out must be a host [B,H,Nq,D] buffer shaped like q");
-    const int64_t rows = host_chunk_rows(q, chunk_rows);
+    const int64_t B = q->shape[0] * q->shape[1];  // (b, h) slices
+    const AdaTensor* others[3] = {k, v, out};
+    for (const AdaTensor* t : others)
+        if (t->shape[0] != q->shape[0] || t->shape[1] != q->shape[1])
+            return fail(ADA_ERR_SHAPE, "batch or head extents differ");
+    const int64_t ro = host_slice_bytes(out);
+    if (ro == 0 || ro != host_slice_bytes(q) || out->dtype != q->dtype)
+        return fail(ADA_ERR_LAYOUT, "out must be a contiguous host [B,H,Nq,D] buffer shaped like q");
+    const int64_t rows = host_chunk_slices(q, chunk_slices);
     size_t ws_bytes = 0, total = 0;
     if ((rc = host_plan(q, k, v, w_down, params, rows, &ws_bytes, &total))) return rc;
     if (device_buffer == nullptr || buffer_bytes < total)
@@ -1078,7 +1085,7 @@ int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v
     HostPipe* hp;
     if ((rc = host_pipe(dev, &hp))) return rc;
     std::lock_guard<std::mutex> pipe_lock(hp->mu);
-    const int64_t rq = host_row_bytes(q), rk = host_row_bytes(k), rv = host_row_bytes(v);
+    const int64_t rq = host_slice_bytes(q), rk = host_slice_bytes(k), rv = host_slice_bytes(v);
     uint8_t* base = static_cast<uint8_t*>(device_buffer);
     const size_t sq = align256(static_cast<size_t>(rq * rows)), sk = align256(static_cast<size_t>(rk * rows)),
                  sv = align256(static_cast<size_t>(rv * rows));

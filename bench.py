@@ -283,7 +283,7 @@ def main():
 
     # End to end through the public API with host buffers: every step copies
     # q, k, v from pinned host memory and the output back, inside the timed
-    # region. ada_attn_fwd_host streams batch-row chunks so the copies in,
+    # region. ada_attn_fwd_host streams chunks of (b, h) slices so the copies in,
     # the forward and the copies out overlap.
     e2e_steps = max(1, min(args.e2e_steps, args.steps))
     hq, hk, hv = (x.contiguous().cpu().pin_memory() for x in (q, k, v))

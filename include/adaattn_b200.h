@@ -175,8 +175,8 @@ int         ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor
 /* ada_attn_fwd for host-resident operands (no counterpart in the reference;
  * the reference's callers pass host tensors and let PyTorch copy them). q, k,
  * v and out point to host memory (pinned for the copies to overlap), each a
- * [B,H,N,D] tensor whose batch rows are contiguous blocks. Batch-row chunks
- * (chunk_rows, or about 32 MB of q per chunk when 0) stream through
+ * contiguous [B,H,N,D] tensor. Chunks of consecutive (b, h) slices
+ * (chunk_slices per chunk, or about 16 MB of q when 0) stream through
  * `device_buffer` (sized by ada_attn_fwd_host_buffer_bytes): copies in, the
  * forward and copies out run on three internal streams, both PCIe
  * directions overlapping each other and the kernels. Every head takes
@@ -186,10 +186,10 @@ int         ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor
  * one device queue one after another on the shared internal streams. */
 size_t      ada_attn_fwd_host_buffer_bytes(const AdaTensor* q, const AdaTensor* k,
                                            const AdaTensor* v, const AdaTensor* w_down,
-                                           const AdaFwdParams* params, int64_t chunk_rows);
+                                           const AdaFwdParams* params, int64_t chunk_slices);
 int         ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v,
                               const AdaTensor* w_down, const AdaFwdParams* params,
-                              AdaTensor* out, int64_t chunk_rows, void* device_buffer,
+                              AdaTensor* out, int64_t chunk_slices, void* device_buffer,
                               size_t buffer_bytes, void* stream);
 
 /* _adaattn_cuda.flash_attention_forward (bindings.cpp:21-68): q, k, v, out are

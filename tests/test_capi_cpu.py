@@ -83,7 +83,7 @@ def test_host_pipeline_checks_layout_before_any_device_work():
 def test_workspace_queries_without_a_gpu():
     """Plan-only queries need no device: the forward workspace grows with the
     FP32 tensor-core operands when FP32 heads of 16-bit inputs are possible,
-    and the host pipeline's staging buffer holds two chunks plus a workspace."""
+    and the host pipeline's staging buffer holds two chunks of slices plus a workspace."""
     import torch
     lib = _lib.load()
     q = torch.zeros(4, 2, 256, 128, dtype=torch.bfloat16)
@@ -98,7 +98,7 @@ def test_workspace_queries_without_a_gpu():
     p.static_precision = 2
     one = lib.ada_attn_fwd_host_buffer_bytes(tq, tq, tq, None, p, 1)
     two = lib.ada_attn_fwd_host_buffer_bytes(tq, tq, tq, None, p, 2)
-    row = 2 * 256 * 128 * 2
-    assert one >= 2 * 4 * row and two >= 2 * 4 * 2 * row and two > one
+    slice_bytes = 256 * 128 * 2  # one (b, h) slice of q
+    assert one >= 2 * 4 * slice_bytes and two >= 2 * 4 * 2 * slice_bytes and two > one
     bad = _lib.tensor(q.transpose(2, 3))
     assert lib.ada_attn_fwd_host_buffer_bytes(bad, tq, tq, None, p, 1) == 0

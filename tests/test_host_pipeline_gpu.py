@@ -1,4 +1,4 @@
-"""Host-resident operands through ada_attn_fwd_host: batch-row chunks copied
+"""Host-resident operands through ada_attn_fwd_host: chunks of (b, h) slices copied
 in, computed and copied out on overlapping streams. Every (b, h) slice is
 computed by the same kernels as the device-resident call, so the results are
 bit-identical to it."""
@@ -18,11 +18,11 @@ def _host(b, h, n, d, dtype, seed):
     return [(torch.randn(b, h, n, d, generator=g)).to(dtype).pin_memory() for _ in range(3)]
 
 
-@pytest.mark.parametrize("chunk_rows", [0, 1, 2])
+@pytest.mark.parametrize("chunk_slices", [0, 1, 4])  # 4: chunks across batch rows, ragged last
 @pytest.mark.parametrize("prec,low", [(PrecisionMode.BF16, False), (PrecisionMode.FP16, True),
                                       (PrecisionMode.FP32, False)])
 @pytest.mark.parametrize("causal", [False, True])
-def test_host_pipeline_matches_device_call(chunk_rows, prec, low, causal, cuda_device):
+def test_host_pipeline_matches_device_call(chunk_slices, prec, low, causal, cuda_device):
     b, h, n, d = 5, 3, 200, 128
     q, k, v = _host(b, h, n, d, torch.bfloat16, seed=31)
     w = None
@@ -34,7 +34,7 @@ def test_host_pipeline_matches_device_call(chunk_rows, prec, low, causal, cuda_d
     scale = 1.0 / math.sqrt(d)
     got = attention_forward_host(q, k, v, scale=scale, causal=causal, static_precision=prec,
                                  static_low_rank=low, w_down=w, device=cuda_device,
-                                 chunk_rows=chunk_rows)
+                                 chunk_slices=chunk_slices)
     torch.cuda.synchronize()
     want = attention_forward(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), scale=scale,
                              causal=causal, static_precision=prec, static_low_rank=low, w_down=w)
