@@ -37,6 +37,12 @@ int launch_target_ranks(const float* eff, int64_t n, int64_t min_rank, int64_t m
 int launch_bounded_wait(uint64_t timeout_ns, unsigned int* status, cudaStream_t stream);
 // Sets the calling thread's ada_get_last_error message; returns `code`.
 int record_last_error(int code, const char* msg);
+// The argument checks of the analyzer entry points (device, tensors, shapes,
+// dtypes, parameters) and the launch description they imply; head_sum is left
+// null for the caller to point at its scratch. Returns ADA_OK or the ADA_ERR_*
+// code, with the message recorded for ada_get_last_error.
+int analyze_setup(const AdaTensor* q, const AdaTensor* k, const AdaAnalyzeParams* params, int32_t* decisions,
+                  float* head_stats, float* summary, AnalyzeLaunch* L);
 // Checks for an sm_100 device and resolves its status word (once per device).
 int device_status_word(unsigned int** status);
 // cuTensorMapEncodeTiled from the driver (resolved once).

@@ -53,44 +53,47 @@ __global__ void __launch_bounds__(kThreads) analyze_stats_kernel(StatsArgs a) {
     const int64_t qbase = b * a.qs[0] + h * a.qs[1];
     const int64_t kbase = b * a.ks[0] + h * a.ks[1];
     if (a.vec) {
-        // 16-byte loads, all of this thread's in flight before the first use
-        // (S * D / 8 <= 1024 groups: at most 4 per thread and tensor).
+        // 16-byte loads in rounds of 4 per thread and tensor, all of a round
+        // in flight before the first use (S * D / 8 groups: one round up to
+        // D = 128, two at D = 256).
         const int g = D >> 3;
         const int n = S * g;
-        uint4 vq[4], vk[4];
+        for (int base = 0; base < n; base += 4 * kThreads) {
+            uint4 vq[4], vk[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int idx = tid + u * kThreads;
-            if (idx < n) {
-                const int r = idx / g, c = (idx - r * g) * 8;
-                const int64_t row = static_cast<int64_t>(r) * a.stride;
-                vq[u] = reinterpret_cast<const uint4*>(a.q)[(qbase + row * a.qs[2] + c) / 8];
-                vk[u] = reinterpret_cast<const uint4*>(a.k)[(kbase + row * a.ks[2] + c) / 8];
+            for (int u = 0; u < 4; ++u) {
+                const int idx = base + tid + u * kThreads;
+                if (idx < n) {
+                    const int r = idx / g, c = (idx - r * g) * 8;
+                    const int64_t row = static_cast<int64_t>(r) * a.stride;
+                    vq[u] = reinterpret_cast<const uint4*>(a.q)[(qbase + row * a.qs[2] + c) / 8];
+                    vk[u] = reinterpret_cast<const uint4*>(a.k)[(kbase + row * a.ks[2] + c) / 8];
+                }
             }
-        }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int idx = tid + u * kThreads;
-            if (idx < n) {
-                const int r = idx / g, c = (idx - r * g) * 8;
-                const uint32_t wq[4] = {vq[u].x, vq[u].y, vq[u].z, vq[u].w};
-                const uint32_t wk[4] = {vk[u].x, vk[u].y, vk[u].z, vk[u].w};
+            for (int u = 0; u < 4; ++u) {
+                const int idx = base + tid + u * kThreads;
+                if (idx < n) {
+                    const int r = idx / g, c = (idx - r * g) * 8;
+                    const uint32_t wq[4] = {vq[u].x, vq[u].y, vq[u].z, vq[u].w};
+                    const uint32_t wk[4] = {vk[u].x, vk[u].y, vk[u].z, vk[u].w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float q0, q1, k0, k1;
-                    if (a.dtype == ADA_BF16) {
-                        q0 = __uint_as_float(wq[i] << 16);
-                        q1 = __uint_as_float(wq[i] & 0xffff0000u);
-                        k0 = __uint_as_float(wk[i] << 16);
-                        k1 = __uint_as_float(wk[i] & 0xffff0000u);
-                    } else {
-                        unpack_f16x2(wq[i], q0, q1);
-                        unpack_f16x2(wk[i], k0, k1);
+                    for (int i = 0; i < 4; ++i) {
+                        float q0, q1, k0, k1;
+                        if (a.dtype == ADA_BF16) {
+                            q0 = __uint_as_float(wq[i] << 16);
+                            q1 = __uint_as_float(wq[i] & 0xffff0000u);
+                            k0 = __uint_as_float(wk[i] << 16);
+                            k1 = __uint_as_float(wk[i] & 0xffff0000u);
+                        } else {
+                            unpack_f16x2(wq[i], q0, q1);
+                            unpack_f16x2(wk[i], k0, k1);
+                        }
+                        sq[r * ld + c + 2 * i] = q0;
+                        sq[r * ld + c + 2 * i + 1] = q1;
+                        sk[r * ld + c + 2 * i] = k0;
+                        sk[r * ld + c + 2 * i + 1] = k1;
                     }
-                    sq[r * ld + c + 2 * i] = q0;
-                    sq[r * ld + c + 2 * i + 1] = q1;
-                    sk[r * ld + c + 2 * i] = k0;
-                    sk[r * ld + c + 2 * i + 1] = k1;
                 }
             }
         }
@@ -543,17 +546,15 @@ constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
 
-// Once per device, with that device current: the device address of the
-// array. In host code the array's name is only a host-side stand-in.
+// Once per device, with that device current (the caller has checked it is an
+// sm_100 device): the device address of the array. In host code the array's
+// name is only a host-side stand-in.
 int noalloc_scratch(float** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
         return record_last_error(ADA_ERR_DEVICE, "ada_analyze_noalloc: no usable current device");
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (g_noalloc_ptr[dev] == nullptr) {
-        cudaDeviceProp prop;
-        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10)
-            return record_last_error(ADA_ERR_DEVICE, "ada_analyze_noalloc: device is not sm_100");
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_head_sum);
         if (e != cudaSuccess || p == nullptr)
@@ -564,72 +565,24 @@ int noalloc_scratch(float** out) {
     return ADA_OK;
 }
 
-bool attn_view_ok(const AdaTensor* t) {
-    if (t == nullptr || t->data == nullptr || t->ndim != 4) return false;
-    if (t->dtype != ADA_F32 && t->dtype != ADA_F16 && t->dtype != ADA_BF16) return false;
-    for (int i = 0; i < 4; ++i)
-        if (t->shape[i] < 0) return false;
-    return true;
-}
-
 }  // namespace
 }  // namespace ada
 
 extern "C" int ada_analyze_noalloc(const AdaTensor* q, const AdaTensor* k, const AdaAnalyzeParams* params,
                                    int32_t* decisions, float* head_stats, float* summary, void* stream) {
     using namespace ada;
-    if (!attn_view_ok(q) || !attn_view_ok(k))
-        return record_last_error(ADA_ERR_INVALID, "ada_analyze_noalloc: q and k must be 4-D float views");
-    if (params == nullptr || decisions == nullptr || head_stats == nullptr || summary == nullptr)
-        return record_last_error(ADA_ERR_INVALID, "ada_analyze_noalloc: null argument");
-    if (q->dtype != k->dtype) return record_last_error(ADA_ERR_DTYPE, "ada_analyze_noalloc: q and k dtypes differ");
-    if (q->shape[0] != k->shape[0] || q->shape[1] != k->shape[1] || q->shape[3] != k->shape[3])
-        return record_last_error(ADA_ERR_SHAPE, "ada_analyze_noalloc: q and k shapes disagree");
-    const int64_t B = q->shape[0], H = q->shape[1], Nq = q->shape[2], Nk = k->shape[2], D = q->shape[3];
-    if (B * H > kNoAllocMaxHeads)
+    AnalyzeLaunch L{};
+    int rc = analyze_setup(q, k, params, decisions, head_stats, summary, &L);
+    if (rc) return rc;
+    // B * H > kNoAllocMaxHeads, tested without forming the product (no overflow)
+    if (L.B > 0 && L.H > kNoAllocMaxHeads / L.B)
         return record_last_error(ADA_ERR_UNSUPPORTED,
                                  "ada_analyze_noalloc: batch * heads exceeds the fixed scratch of 65536 "
                                  "heads; use ada_analyze with a workspace");
-    if (D < 1 || D > 256) return record_last_error(ADA_ERR_UNSUPPORTED, "ada_analyze_noalloc: head dim outside [1, 256]");
-    if (Nq < 1 || Nk < 1) return record_last_error(ADA_ERR_SHAPE, "ada_analyze_noalloc: empty sequence");
-    if (params->default_precision < 0 || params->default_precision > 4)
-        return record_last_error(ADA_ERR_INVALID, "ada_analyze_noalloc: default precision out of range");
     float* head_sum = nullptr;
-    const int rc = noalloc_scratch(&head_sum);
-    if (rc != ADA_OK) return rc;
-    if (B * H == 0) return ADA_OK;
-    const int stride = params->sample_stride > 1 ? params->sample_stride : 1;
-    const int64_t n_min = Nq < Nk ? Nq : Nk;
-    int64_t S = (n_min + stride - 1) / stride;
-    if (S > 64) S = 64;
-    AnalyzeLaunch L{};
-    L.q = q->data;
-    L.k = k->data;
-    L.dtype = q->dtype;
-    L.B = B;
-    L.H = H;
-    L.Nq = Nq;
-    L.Nk = Nk;
-    L.D = D;
-    for (int i = 0; i < 4; ++i) {
-        L.qs[i] = q->stride[i];
-        L.ks[i] = k->stride[i];
-    }
-    L.scale = params->scale;
-    L.eps = params->eps;
-    L.log_s = std::log(static_cast<double>(S));
-    L.S = static_cast<int>(S);
-    L.stride = stride;
-    L.head_stats = head_stats;
+    if ((rc = noalloc_scratch(&head_sum)) != ADA_OK) return rc;
+    if (L.B * L.H == 0) return ADA_OK;
     L.head_sum = head_sum;
-    L.decisions = decisions;
-    L.summary = summary;
-    L.rank_threshold = params->rank_threshold;
-    L.enable_rank = params->enable_adaptive_rank;
-    L.enable_prec = params->enable_adaptive_precision;
-    L.default_prec = params->default_precision;
-    L.allow_fp8 = params->allow_fp8;
-    L.granularity = params->granularity;
     if (launch_analyze(L, static_cast<cudaStream_t>(stream)) != ADA_OK)
         return record_last_error(ADA_ERR_LAUNCH, "ada_analyze_noalloc: launch failed");
     return ADA_OK;

@@ -446,6 +446,55 @@ void copy_strides(int64_t* dst, const AdaTensor* t) {
 namespace ada {
 // Lets entry points defined in other files report through ada_get_last_error.
 int record_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+int analyze_setup(const AdaTensor* q, const AdaTensor* k, const AdaAnalyzeParams* params, int32_t* decisions,
+                  float* head_stats, float* summary, AnalyzeLaunch* L) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if ((rc = check_attn_tensor(q, "q")) || (rc = check_attn_tensor(k, "k"))) return rc;
+    if (params == nullptr || decisions == nullptr || head_stats == nullptr || summary == nullptr)
+        return fail(ADA_ERR_INVALID, "null argument");
+    if (q->dtype != k->dtype) return fail(ADA_ERR_DTYPE, "q and k dtypes differ");
+    if (q->shape[0] != k->shape[0] || q->shape[1] != k->shape[1] || q->shape[3] != k->shape[3])
+        return fail(ADA_ERR_SHAPE, "q and k shapes disagree");
+    const int64_t B = q->shape[0], H = q->shape[1], Nq = q->shape[2], Nk = k->shape[2], D = q->shape[3];
+    if (D < 1 || D > 256) return fail(ADA_ERR_UNSUPPORTED, "analyzer head dim %lld outside [1, 256]", (long long)D);
+    if (Nq < 1 || Nk < 1) return fail(ADA_ERR_SHAPE, "empty sequence: the sample size would be 0");
+    if (params->default_precision < 0 || params->default_precision > 4)
+        return fail(ADA_ERR_INVALID, "default precision %d", params->default_precision);
+    const int stride = params->sample_stride > 1 ? params->sample_stride : 1;
+    const int64_t n_min = Nq < Nk ? Nq : Nk;
+    int64_t S = (n_min + stride - 1) / stride;
+    if (S > 64) S = 64;
+    *L = AnalyzeLaunch{};
+    L->q = q->data;
+    L->k = k->data;
+    L->dtype = q->dtype;
+    L->B = B;
+    L->H = H;
+    L->Nq = Nq;
+    L->Nk = Nk;
+    L->D = D;
+    copy_strides(L->qs, q);
+    copy_strides(L->ks, k);
+    L->scale = params->scale;
+    L->eps = params->eps;
+    L->log_s = std::log(static_cast<double>(S));
+    L->S = static_cast<int>(S);
+    L->stride = stride;
+    L->head_stats = head_stats;
+    L->head_sum = nullptr;
+    L->decisions = decisions;
+    L->summary = summary;
+    L->rank_threshold = params->rank_threshold;
+    L->enable_rank = params->enable_adaptive_rank;
+    L->enable_prec = params->enable_adaptive_precision;
+    L->default_prec = params->default_precision;
+    L->allow_fp8 = params->allow_fp8;
+    L->granularity = params->granularity;
+    return ADA_OK;
+}
 int device_status_word(unsigned int** status) { return device_setup(status); }
 int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) { return encoder(fn); }
 uint64_t default_wait_timeout_ns() { return wait_timeout_ns(); }
@@ -579,53 +628,13 @@ size_t ada_analyze_workspace_bytes(int64_t batch, int64_t heads) {
 
 int ada_analyze(const AdaTensor* q, const AdaTensor* k, const AdaAnalyzeParams* params, int32_t* decisions,
                 float* head_stats, float* summary, void* workspace, size_t workspace_bytes, void* stream) {
-    unsigned int* st;
-    int rc = device_setup(&st);
-    if (rc) return rc;
-    if ((rc = check_attn_tensor(q, "q")) || (rc = check_attn_tensor(k, "k"))) return rc;
-    if (params == nullptr || decisions == nullptr || head_stats == nullptr || summary == nullptr)
-        return fail(ADA_ERR_INVALID, "null argument");
-    if (q->dtype != k->dtype) return fail(ADA_ERR_DTYPE, "q and k dtypes differ");
-    if (q->shape[0] != k->shape[0] || q->shape[1] != k->shape[1] || q->shape[3] != k->shape[3])
-        return fail(ADA_ERR_SHAPE, "q and k shapes disagree");
-    const int64_t B = q->shape[0], H = q->shape[1], Nq = q->shape[2], Nk = k->shape[2], D = q->shape[3];
-    if (D < 1 || D > 256) return fail(ADA_ERR_UNSUPPORTED, "analyzer head dim %lld outside [1, 256]", (long long)D);
-    if (Nq < 1 || Nk < 1) return fail(ADA_ERR_SHAPE, "empty sequence: the sample size would be 0");
-    const int stride = params->sample_stride > 1 ? params->sample_stride : 1;
-    const int64_t n_min = Nq < Nk ? Nq : Nk;
-    int64_t S = (n_min + stride - 1) / stride;
-    if (S > 64) S = 64;
-    if (B * H == 0) return ADA_OK;
-    if (workspace_bytes < ada_analyze_workspace_bytes(B, H) || workspace == nullptr)
-        return fail(ADA_ERR_WORKSPACE, "analyzer workspace too small");
-    if (params->default_precision < 0 || params->default_precision > 4)
-        return fail(ADA_ERR_INVALID, "default precision %d", params->default_precision);
     AnalyzeLaunch L{};
-    L.q = q->data;
-    L.k = k->data;
-    L.dtype = q->dtype;
-    L.B = B;
-    L.H = H;
-    L.Nq = Nq;
-    L.Nk = Nk;
-    L.D = D;
-    copy_strides(L.qs, q);
-    copy_strides(L.ks, k);
-    L.scale = params->scale;
-    L.eps = params->eps;
-    L.log_s = std::log(static_cast<double>(S));
-    L.S = static_cast<int>(S);
-    L.stride = stride;
-    L.head_stats = head_stats;
+    int rc = analyze_setup(q, k, params, decisions, head_stats, summary, &L);
+    if (rc) return rc;
+    if (L.B * L.H == 0) return ADA_OK;
+    if (workspace_bytes < ada_analyze_workspace_bytes(L.B, L.H) || workspace == nullptr)
+        return fail(ADA_ERR_WORKSPACE, "analyzer workspace too small");
     L.head_sum = static_cast<float*>(workspace);
-    L.decisions = decisions;
-    L.summary = summary;
-    L.rank_threshold = params->rank_threshold;
-    L.enable_rank = params->enable_adaptive_rank;
-    L.enable_prec = params->enable_adaptive_precision;
-    L.default_prec = params->default_precision;
-    L.allow_fp8 = params->allow_fp8;
-    L.granularity = params->granularity;
     rc = launch_analyze(L, static_cast<cudaStream_t>(stream));
     return rc ? fail(rc, "analyzer launch failed: %s", cudaGetErrorString(cudaGetLastError())) : ADA_OK;
 }
@@ -1100,6 +1109,15 @@ int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v
         (rc = ck(cudaStreamWaitEvent(hp->s_comp, hp->start, 0), "stream wait")) ||
         (rc = ck(cudaStreamWaitEvent(hp->s_out, hp->start, 0), "stream wait")))
         return rc;
+    // After a failure part-way through, work already queued on the internal
+    // streams keeps running: the caller's stream waits for all of it, so the
+    // caller may reuse device_buffer and the host buffers once `stream` is done.
+    auto join_on_error = [&](int code) {
+        cudaStream_t internal[3] = {hp->s_in, hp->s_comp, hp->s_out};
+        for (cudaStream_t s : internal)
+            if (cudaEventRecord(hp->start, s) == cudaSuccess) cudaStreamWaitEvent(caller, hp->start, 0);
+        return code;
+    };
     const int64_t nchunks = (B + rows - 1) / rows;
     int last = 0;
     for (int64_t c = 0; c < nchunks; ++c) {
@@ -1110,7 +1128,7 @@ int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v
         uint8_t* dv = dk + sk;
         uint8_t* dout = dv + sv;
         // copy in once the forward two chunks back has read this slot
-        if (c >= 2 && (rc = ck(cudaStreamWaitEvent(hp->s_in, hp->comp[sl], 0), "stream wait"))) return rc;
+        if (c >= 2 && (rc = ck(cudaStreamWaitEvent(hp->s_in, hp->comp[sl], 0), "stream wait"))) return join_on_error(rc);
         if ((rc = ck(cudaMemcpyAsync(dq, static_cast<const uint8_t*>(q->data) + r0 * rq, n * rq,
                                      cudaMemcpyHostToDevice, hp->s_in), "copy of q")) ||
             (rc = ck(cudaMemcpyAsync(dk, static_cast<const uint8_t*>(k->data) + r0 * rk, n * rk,
@@ -1118,22 +1136,22 @@ int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v
             (rc = ck(cudaMemcpyAsync(dv, static_cast<const uint8_t*>(v->data) + r0 * rv, n * rv,
                                      cudaMemcpyHostToDevice, hp->s_in), "copy of v")) ||
             (rc = ck(cudaEventRecord(hp->in[sl], hp->s_in), "event record")))
-            return rc;
+            return join_on_error(rc);
         // forward once the inputs landed and the copy out two chunks back has read the output slot
-        if ((rc = ck(cudaStreamWaitEvent(hp->s_comp, hp->in[sl], 0), "stream wait"))) return rc;
-        if (c >= 2 && (rc = ck(cudaStreamWaitEvent(hp->s_comp, hp->out[sl], 0), "stream wait"))) return rc;
+        if ((rc = ck(cudaStreamWaitEvent(hp->s_comp, hp->in[sl], 0), "stream wait"))) return join_on_error(rc);
+        if (c >= 2 && (rc = ck(cudaStreamWaitEvent(hp->s_comp, hp->out[sl], 0), "stream wait"))) return join_on_error(rc);
         AdaTensor cq = chunk_view(q, dq, n), ckt = chunk_view(k, dk, n), cv = chunk_view(v, dv, n),
                   co = chunk_view(out, dout, n);
         if ((rc = ada_attn_fwd(&cq, &ckt, &cv, w_down, nullptr, nullptr, params, 0, params->static_low_rank, &co,
                                ws, ws_bytes, hp->s_comp)))
-            return rc;
-        if ((rc = ck(cudaEventRecord(hp->comp[sl], hp->s_comp), "event record"))) return rc;
+            return join_on_error(rc);
+        if ((rc = ck(cudaEventRecord(hp->comp[sl], hp->s_comp), "event record"))) return join_on_error(rc);
         // copy out
         if ((rc = ck(cudaStreamWaitEvent(hp->s_out, hp->comp[sl], 0), "stream wait")) ||
             (rc = ck(cudaMemcpyAsync(static_cast<uint8_t*>(out->data) + r0 * ro, dout, n * ro,
                                      cudaMemcpyDeviceToHost, hp->s_out), "copy of out")) ||
             (rc = ck(cudaEventRecord(hp->out[sl], hp->s_out), "event record")))
-            return rc;
+            return join_on_error(rc);
         last = sl;
     }
     // the caller's stream continues after the last copy out (copies out run in order)

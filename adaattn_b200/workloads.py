@@ -10,8 +10,8 @@ Workloads (tensors are [B, H, N, D] unless noted):
                  exp(U[ln 0.25, ln 4]) so heads span high and low entropy.
   dense_bf16     B8 H32 N4096 D128 bf16 causal, iid N(0,1)/sqrt(D).
   low_rank_mix   B4 H16 N8192 D128 bf16 non-causal; heads [0, H/2) have
-                 K = A B^T / sqrt(32) (inner rank 32) + 0.01 N(0,1), the
-                 rest are full-rank N(0,1).
+                 K = A B^T (A, B N(0,1) with inner rank 32) + 0.01 N(0,1),
+                 the rest are full-rank N(0,1).
   precision_mix  B8 H32 N2048 D128 bf16 causal; each (b, h) draws a scale
                  from {0.1, 1, 10, 100} and Q, K, V are N(0,1) * scale.
   gpt2_small     token ids [16, 1024] uniform over a 50257 vocabulary for a
@@ -100,7 +100,7 @@ def make_qkv(w: Workload, seed: int = 0, device: str = "cpu"
         inner = 32
         a = _randn((w.batch, half, w.seq, inner), g, device)
         bm = _randn((w.batch, half, w.head_dim, inner), g, device)
-        low = torch.matmul(a, bm.transpose(-2, -1)) / math.sqrt(inner)
+        low = torch.matmul(a, bm.transpose(-2, -1))
         k[:, :half] = low + 0.01 * k[:, :half]
     elif w.kind == "scale_mix":
         choices = torch.tensor([0.1, 1.0, 10.0, 100.0], device=device)

@@ -7,10 +7,14 @@ batch, inputs resident in HBM (805 MB > L2, so no flush is needed).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Multi-GPU (torchrun, one process per GPU): weak scaling by (batch x head)
-shards -- every rank processes its own B8 H32 slice of a job N times larger,
-no collective inside the timed attention; an NCCL all-gather of outputs is
-timed separately afterwards. Rank 0 prints one JSON line.
+Multi-GPU (torchrun, one process per GPU): strong scaling by (batch x head)
+shards -- the 256 (b, h) units of the one B8 H32 job are split into
+contiguous ranges, one per rank, with no collective inside the timed
+attention; the NCCL all-gather of the outputs is timed separately afterwards
+(``--scaling weak`` gives every rank its own B8 H32 job instead). The time of
+a step is the maximum over ranks; rank 0 prints one JSON line, with every
+rank's kernel time. A second leg times the GPT-2-small-shaped decoder with
+AdaAttention in every layer, its batch of 16 split over the ranks.
 
 --impl reference times the reference algorithm's CPU implementation (the
 oracle's restatement of AdaAttention._compute_dense_attention) on the host
@@ -127,15 +131,18 @@ def dist_env():
     return world, rank, local
 
 
+SAMPLE_HEADS = 4  # heads of batch row 0 in one host-core sample
+
+
 def cpu_sample(workload, seconds: float = 10.0, max_reps: int = 50):
     """Time the oracle's dense BF16 attention on a slice of the workload.
 
-    Sample: batch row 0, `heads` heads, full sequence; repeated until about
-    `seconds` of CPU work. Returns (TFLOP/s, threads, description)."""
+    Sample: batch row 0, SAMPLE_HEADS heads, full sequence; repeated until
+    about `seconds` of CPU work. Returns (TFLOP/s, threads, description)."""
     import oracle as O
     from adaattn_b200.workloads import make_qkv
     torch.set_num_threads(os.cpu_count() or 1)
-    heads = 4
+    heads = SAMPLE_HEADS
     w = workload.scaled(batch=1, heads=heads)
     q, k, v = make_qkv(w, seed=0)
     flops = w.dense_flops()
@@ -169,13 +176,23 @@ def run_reference(args, workload):
             vals.append(v)
     value = statistics.median(vals)
     flops = workload.dense_flops()
+    sample_heads = SAMPLE_HEADS
+    sample_flops = workload.scaled(batch=1, heads=sample_heads).dense_flops()
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": flops / (value * 1e12) * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong" if args.scaling == "strong" else "weak", "vs_baseline": None,
+        "dtype": "bf16",
         "data": "synthetic: seeded N(0,1)/sqrt(D) bf16",
-        "config": workload_config(workload, args.gpus),
+        "config": workload_config(workload, args.gpus, args.scaling),
+        # Each step times a slice of the workload; ms_per_step is that slice's
+        # measured time scaled to the full job by its share of the FLOPs
+        # ((b, h) slices are independent and equally costly).
+        "extrapolated": True,
+        "slice": f"batch row 0, {sample_heads} of {workload.heads} heads, N={workload.seq}, "
+                 f"{sample_flops / flops:.5f} of the job's FLOPs",
+        "measured_ms_per_slice": sample_flops / (value * 1e12) * 1e3,
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": desc + ("; the host cores of one node, so the same value at "
                                            "every GPU count" if args.gpus > 1 else "")},
@@ -187,13 +204,72 @@ def run_reference(args, workload):
     return 0
 
 
-def workload_config(w, n):
+def workload_config(w, n, scaling):
+    units = w.batch * w.heads
+    if scaling == "strong":
+        par = (f"(batch x head) shards: the {units} (b, h) units of one job split over {n} "
+               f"GPU(s), contiguous ranges, no collective in attention; outputs all-gathered "
+               f"over NCCL afterwards, timed separately")
+        batch = w.batch
+    else:
+        par = (f"(batch x head) shards, weak scaling: each of {n} GPU(s) processes its own "
+               f"B{w.batch} H{w.heads} job; no collective in attention")
+        batch = w.batch * n
     return {"workload": f"dense_bf16 causal attention B{w.batch} H{w.heads} N{w.seq} "
                         f"D{w.head_dim}, precision forced BF16, rank forced dense",
-            "batch_per_gpu": w.batch, "global_batch": w.batch * n, "heads": w.heads,
-            "seq_len": w.seq, "head_dim": w.head_dim, "causal": w.causal,
-            "parallelism": f"(batch x head) shards, {n} GPU(s), no collective in attention",
-            "l2": "inputs 805 MB per GPU > 126 MB L2 (no flush needed)"}
+            "global_batch": batch, "heads": w.heads, "seq_len": w.seq, "head_dim": w.head_dim,
+            "causal": w.causal, "parallelism": par,
+            "l2": "inputs 805 MB per job > 126 MB L2 (no flush needed)"}
+
+
+def gpt2_leg(dev, world, rank, barrier, steps=10):
+    """GPT-2-small-shaped decoder with AdaAttention in every layer (12 layers,
+    E768, H12, FF3072, seq 1024, batch 16, weights N(0, 0.02), bf16): forward
+    tokens/s, the batch split over the ranks (replicated weights, no
+    collective in the forward)."""
+    from adaattn_b200 import AdaAttention
+    from adaattn_b200.host_model import AdaptiveTransformer
+    from adaattn_b200.shard import shard_range
+    from adaattn_b200.workloads import GPT2_SMALL as c, make_token_ids
+    torch.manual_seed(0)
+    model = AdaptiveTransformer(vocab_size=c["vocab"], embed_dim=c["embed_dim"],
+                                num_heads=c["num_heads"], num_layers=c["num_layers"],
+                                ff_dim=c["ff_dim"], max_seq_len=c["seq"], dropout=0.0)
+    model.init_gpt2_weights(std=0.02)
+    for m in model.modules():
+        if isinstance(m, AdaAttention):
+            m.config.enable_nan_check = False
+    model = model.to(dev).to(torch.bfloat16).eval()
+    ids = make_token_ids(c["batch"], c["seq"], c["vocab"], seed=0, device=str(dev))
+    lo, hi = shard_range(c["batch"], rank, world)
+    local = ids[lo:hi]
+
+    def step():
+        with torch.no_grad():
+            return model(local)
+
+    for _ in range(3):
+        step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    barrier()
+    ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item()) / steps
+    stats = model.get_attention_statistics()[0]
+    del model
+    return {"workload": f"gpt2_small decoder B{c['batch']} N{c['seq']} E{c['embed_dim']} "
+                        f"H{c['num_heads']} L{c['num_layers']} bf16, batch split over {world} GPU(s)",
+            "tokens_per_s": c["batch"] * c["seq"] / (ms * 1e-3), "ms_per_forward": ms,
+            "sequences_per_gpu": hi - lo, "steps": steps,
+            "attention_precision_layer0": stats["precision_distribution"]}
 
 
 def main():
@@ -202,8 +278,11 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong: one B8 H32 job split over the GPUs (default); weak: a job per GPU")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpt2", action="store_true", help="skip the GPT-2-small leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="profiling only: smaller batch than the B8 workload")
     ap.add_argument("--heads", type=int, default=None,
@@ -219,6 +298,7 @@ def main():
     import torch.distributed as dist
     from adaattn_b200 import PrecisionMode, attention_forward, attention_forward_host
     from adaattn_b200.core import host_buffer_bytes
+    from adaattn_b200.shard import gather_slices, local_slices, shard_range
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -229,13 +309,24 @@ def main():
 
     w = workload
     scale = 1.0 / math.sqrt(w.head_dim)
-    q, k, v = make_qkv(w, seed=1000 + rank, device=str(dev))
-    out = torch.empty(w.batch, w.seq, w.heads, w.head_dim, dtype=w.dtype, device=dev)
-    out_v = out.transpose(1, 2)
+    strong = args.scaling == "strong"
+    if strong:
+        # every rank draws the same job and keeps its contiguous range of (b, h) units
+        qf, kf, vf = make_qkv(w, seed=1000, device=str(dev))
+        q, k, v = (local_slices(x, rank, world).contiguous() for x in (qf, kf, vf))
+        del qf, kf, vf
+        u0, u1 = shard_range(w.batch * w.heads, rank, world)
+        units_total = w.batch * w.heads
+    else:
+        q, k, v = make_qkv(w, seed=1000 + rank, device=str(dev))
+        u0, u1 = 0, w.batch * w.heads
+        units_total = world * w.batch * w.heads
+    torch.cuda.empty_cache()
+    out = torch.empty(q.shape, dtype=w.dtype, device=dev)
 
     def step():
         attention_forward(q, k, v, scale=scale, causal=w.causal,
-                          static_precision=PrecisionMode.BF16, out=out_v)
+                          static_precision=PrecisionMode.BF16, out=out)
 
     for _ in range(args.warmup):
         step()
@@ -255,36 +346,43 @@ def main():
             step()
         stop.record()
         barrier()
-    ms_total = start.elapsed_time(stop)
-    t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+    ms_rank = start.elapsed_time(stop)
+    per_rank = torch.tensor([ms_rank / args.steps], device=dev, dtype=torch.float64)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total = float(t.item())
-    ms_per_step = ms_total / args.steps
-    flops = w.dense_flops()
-    value = world * flops * args.steps / (ms_total * 1e-3) / 1e12
-    tokens_per_s = world * w.tokens * args.steps / (ms_total * 1e-3)
+        gathered_ms = [torch.empty_like(per_rank) for _ in range(world)]
+        dist.all_gather(gathered_ms, per_rank)
+        per_rank_ms = [float(x.item()) for x in gathered_ms]
+    else:
+        per_rank_ms = [float(per_rank.item())]
+    ms_per_step = max(per_rank_ms)
+    unit_flops = w.dense_flops() / (w.batch * w.heads)   # every (b, h) unit costs the same
+    job_flops = unit_flops * units_total
+    value = job_flops / (ms_per_step * 1e-3) / 1e12
+    tokens_per_s = (units_total // w.heads) * w.seq / (ms_per_step * 1e-3)
 
     # NCCL all-gather of the outputs (outside the timed attention region).
     allgather_ms = None
     if world > 1:
-        gathered = torch.empty(world, *out.shape, dtype=out.dtype, device=dev)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        dist.all_gather_into_tensor(gathered, out)
+        if strong:
+            full = gather_slices(out, w.batch, w.heads)
+        else:
+            full = torch.empty(world, *out.shape, dtype=out.dtype, device=dev)
+            dist.all_gather_into_tensor(full, out)
         e1.record()
         barrier()
         ag = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
         dist.all_reduce(ag, op=dist.ReduceOp.MAX)
         allgather_ms = float(ag.item())
-        del gathered
+        del full
 
     # End to end through the public API with host buffers: every step copies
-    # q, k, v from pinned host memory and the output back, inside the timed
-    # region. ada_attn_fwd_host streams chunks of (b, h) slices so the copies in,
-    # the forward and the copies out overlap.
+    # this rank's q, k, v from pinned host memory and the output back, inside
+    # the timed region. ada_attn_fwd_host streams chunks of (b, h) slices so
+    # the copies in, the forward and the copies out overlap.
     e2e_steps = max(1, min(args.e2e_steps, args.steps))
     hq, hk, hv = (x.contiguous().cpu().pin_memory() for x in (q, k, v))
     hout = torch.empty(hq.shape, dtype=out.dtype).pin_memory()
@@ -307,37 +405,50 @@ def main():
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_ms.item())
-    e2e_value = world * flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    e2e_value = job_flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
     h2d = sum(x.numel() * x.element_size() for x in (q, k, v))
     d2h = out.numel() * out.element_size()
+    del hq, hk, hv, hout, stage, q, k, v, out
+    torch.cuda.empty_cache()
+
+    gpt2 = None if args.no_gpt2 else gpt2_leg(dev, world, rank, barrier)
 
     if world > 1:
         dist.barrier()
     if rank == 0:
         peaks, src = load_peaks()
         peak = float(peaks["bf16_tflops"])
-        achieved = flops / (ms_per_step * 1e-3) / 1e12
+        # roofline of one GPU's kernel: its own units over its own time
+        local_flops = unit_flops * (u1 - u0)
+        achieved = local_flops / (per_rank_ms[0] * 1e-3) / 1e12
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic: seeded N(0,1)/sqrt(D) bf16",
-            "config": workload_config(w, world),
+            "config": workload_config(w, world, args.scaling),
             "tokens_per_s": tokens_per_s,
             "pct_of_bf16_peak": 100.0 * achieved / peak,
+            "per_rank_ms": per_rank_ms,
+            "units_per_rank": [shard_range(w.batch * w.heads, r, world) for r in range(world)]
+            if strong else None,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{src} bf16_tflops (burst)",
-                         "traffic": profiled_traffic(),
-                         "algorithmic_flops_per_launch": flops},
+                         "traffic": profiled_traffic() if world == 1 else None,
+                         "algorithmic_flops_per_launch": local_flops},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "ms_per_step": e2e_ms / e2e_steps},
+                    "ms_per_step": e2e_ms / e2e_steps,
+                    "note": "per rank: its own (b, h) units through ada_attn_fwd_host"},
             "gpu_launches": args.steps,
             "clocks": clk.summary(),
         }
         if allgather_ms is not None:
             line["allgather_outputs_ms"] = allgather_ms
+        if gpt2 is not None:
+            line["gpt2_small"] = gpt2
         if not args.no_cpu_baseline and world == 1:  # the host-core baseline is an N=1 figure
             v_cpu, cores, desc = cpu_sample(w)
             line["cpu_baseline"] = {"value": v_cpu, "unit": "TFLOP/s", "cores": cores,

@@ -182,8 +182,11 @@ int         ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor
  * directions overlapping each other and the kernels. Every head takes
  * params->static_precision / static_low_rank (w_down on the device when
  * low rank); no mask. Ordered after prior work on `stream`, which waits for
- * the last copy out: `out` is complete once `stream` is. Concurrent calls on
- * one device queue one after another on the shared internal streams. */
+ * the last copy out: `out` is complete once `stream` is, also when the call
+ * fails part-way through. Calls on one device enqueue one at a time on the
+ * shared internal streams; a device_buffer must not be shared by calls on
+ * different streams (nothing orders one call's first copy into it after the
+ * other call's last read of it). */
 size_t      ada_attn_fwd_host_buffer_bytes(const AdaTensor* q, const AdaTensor* k,
                                            const AdaTensor* v, const AdaTensor* w_down,
                                            const AdaFwdParams* params, int64_t chunk_slices);

@@ -35,6 +35,8 @@ __all__ = [
     "module_forward",
     "fp8_quantize_tiles", "fp8_dense_attention", "randomized_svd",
     "rsvd_sketch", "E4M3_MAX", "FP8_TILE",
+    "kernel_flash_attention_forward", "kernel_adaptive_attention_forward",
+    "compute_entropy", "estimate_effective_rank", "determine_target_ranks",
 ]
 
 FP32, FP16, BF16, FP8, AUTO = 0, 1, 2, 3, 4
@@ -212,31 +214,41 @@ def _softmax_in_precision(scores: torch.Tensor, prec: int, dt: torch.dtype
 
 
 def dense_attention(q, k, v, prec: int, scale: float, causal: bool,
-                    attention_mask=None) -> torch.Tensor:
+                    attention_mask=None, cast_back: bool = True,
+                    compute: Optional[torch.dtype] = None) -> torch.Tensor:
     """Dense branch, src/adaattn/attention/adaattn.py:291-339 (eval mode).
 
     Scores are clamped to the fp16 range for FP16 and FP8 (:309-310).
+    cast_back=False returns the result in the compute dtype, before the
+    reference's final cast to the inputs' dtype (:339). ``compute`` replaces
+    the precision's compute dtype (float64 gives the exact value the FP32
+    branch approximates).
     """
-    dt = compute_dtype(prec)
+    dt = compute or compute_dtype(prec)
     qc, kc, vc = q.to(dt), k.to(dt), v.to(dt)
     scores = torch.matmul(qc, kc.transpose(-2, -1)) * scale
     if prec in (FP16, FP8):
         scores = torch.clamp(scores, min=-65504, max=65504)
     scores = apply_masks(scores, causal, attention_mask, dt)
     probs = _softmax_in_precision(scores, prec, dt)
-    return torch.matmul(probs, vc).to(q.dtype)
+    out = torch.matmul(probs, vc)
+    return out.to(q.dtype) if cast_back else out
 
 
 def low_rank_attention(q, k, v, w_down: torch.Tensor, prec: int, scale: float,
-                       causal: bool, attention_mask=None) -> torch.Tensor:
+                       causal: bool, attention_mask=None, cast_back: bool = True,
+                       compute: Optional[torch.dtype] = None) -> torch.Tensor:
     """Low-rank branch, src/adaattn/attention/adaattn.py:341-394 (eval mode).
 
     q and k go through the learned head-dim projection ``rank_proj_down``
     (weight [r, D], no bias) in the inputs' dtype, then scores use the
     module's 1/sqrt(D) scale on the r-dimensional products; V stays full
-    width. No clamp on this branch.
+    width. No clamp on this branch. cast_back=False returns the result in
+    the compute dtype, before the final cast to the inputs' dtype (:394);
+    ``compute`` replaces the compute dtype as in dense_attention (the
+    projection stays in the inputs' dtype).
     """
-    dt = compute_dtype(prec)
+    dt = compute or compute_dtype(prec)
     w = w_down.to(q.dtype)
     q_low = F.linear(q, w).to(dt)
     k_low = F.linear(k, w).to(dt)
@@ -244,7 +256,8 @@ def low_rank_attention(q, k, v, w_down: torch.Tensor, prec: int, scale: float,
     scores = torch.matmul(q_low, k_low.transpose(-2, -1)) * scale
     scores = apply_masks(scores, causal, attention_mask, dt)
     probs = _softmax_in_precision(scores, prec, dt)
-    return torch.matmul(probs, vc).to(q.dtype)
+    out = torch.matmul(probs, vc)
+    return out.to(q.dtype) if cast_back else out
 
 
 def _slice_mask(mask, b: int, h: int):
@@ -428,3 +441,75 @@ def rsvd_sketch(shape_batch, n: int, rank: int, m: int, seed: int,
     k = min(rank + oversample, min(m, n))
     g = torch.Generator().manual_seed(seed)
     return torch.randn(*shape_batch, n, k, generator=g, dtype=dtype)
+
+
+# --------------------------------------------------------------------------
+# Kernel-level ops of the reference's native module _adaattn_cuda
+# (src/adaattn/kernels/bindings.cpp:21-135) and the Python fallbacks that
+# adaattn.kernels runs when that module is absent (kernels/__init__.py:81-213).
+# Tensors are [B, N, H, D] here, as in those functions.
+# --------------------------------------------------------------------------
+
+def kernel_flash_attention_forward(q, k, v, softmax_scale: Optional[float] = None,
+                                   causal: bool = False) -> torch.Tensor:
+    """flash_attention_forward: bindings.cpp:21-68, kernels/__init__.py:81-120.
+
+    Scores, softmax and P.V in the tensors' own dtype, causal mask
+    triu(ones(N, N), 1) filled with -inf; returns [B, N, H, D].
+    """
+    n = q.shape[1]
+    scale = softmax_scale if softmax_scale is not None else q.shape[-1] ** -0.5
+    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    scores = torch.matmul(qt, kt.transpose(-2, -1)) * scale
+    if causal:
+        mask = torch.triu(torch.ones(n, n, dtype=torch.bool), diagonal=1)
+        scores = scores.masked_fill(mask, float("-inf"))
+    probs = torch.softmax(scores, dim=-1)
+    return torch.matmul(probs, vt).transpose(1, 2)
+
+
+_KERNEL_PRECISION = {"fp16": torch.float16, "bf16": torch.bfloat16}
+
+
+def kernel_adaptive_attention_forward(q, k, v, precision: str = "fp16",
+                                      softmax_scale: Optional[float] = None,
+                                      causal: bool = False) -> torch.Tensor:
+    """adaptive_attention_forward, dense branch (target_rank None):
+    kernels/__init__.py:151-213.
+
+    Cast to the requested precision ("fp16", "bf16", anything else fp32),
+    softmax taken in fp32 and cast back, result cast to the inputs' dtype.
+    (The native binding, bindings.cpp:73-96, ignores target_rank; the Python
+    fallback's low-rank branch draws a fresh random projection per call and
+    has no fixed answer to restate.)
+    """
+    orig = q.dtype
+    dt = _KERNEL_PRECISION.get(precision, torch.float32)
+    n = q.shape[1]
+    scale = softmax_scale if softmax_scale is not None else q.shape[-1] ** -0.5
+    qt, kt, vt = (t.to(dt).transpose(1, 2) for t in (q, k, v))
+    scores = torch.matmul(qt, kt.transpose(-2, -1)) * scale
+    if causal:
+        mask = torch.triu(torch.ones(n, n, dtype=torch.bool), diagonal=1)
+        scores = scores.masked_fill(mask, float("-inf"))
+    probs = torch.softmax(scores.float(), dim=-1).to(dt)
+    return torch.matmul(probs, vt).transpose(1, 2).to(orig)
+
+
+def compute_entropy(attn_weights: torch.Tensor) -> torch.Tensor:
+    """-(w * log(w + 1e-10)).sum(-1): bindings.cpp:101-109."""
+    return -(attn_weights * torch.log(attn_weights + 1e-10)).sum(-1)
+
+
+def estimate_effective_rank(attn_weights: torch.Tensor) -> torch.Tensor:
+    """exp(mean(entropy, -1)): bindings.cpp:114-118."""
+    return torch.exp(compute_entropy(attn_weights).mean(-1))
+
+
+def determine_target_ranks(effective_rank: torch.Tensor, min_rank: int = 8,
+                           max_rank: int = 128, threshold: float = 32.0) -> torch.Tensor:
+    """where(rank < threshold, (rank * 1.5).clamp(min, max) as int64, max_rank):
+    bindings.cpp:123-135 (defaults from :183-188)."""
+    return torch.where(effective_rank < threshold,
+                       (effective_rank * 1.5).clamp(min_rank, max_rank).to(torch.int64),
+                       torch.full_like(effective_rank, max_rank).to(torch.int64))

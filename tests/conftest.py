@@ -20,3 +20,16 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.fail("GPU test collected on a machine without a CUDA device")
     return torch.device("cuda:0")
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """Measured max-abs errors of the parity checks, per precision."""
+    try:
+        import parity
+    except Exception:
+        return
+    lines = parity.summary_lines()
+    if lines:
+        terminalreporter.write_sep("-", "parity: measured max-abs error per precision")
+        for line in lines:
+            terminalreporter.write_line(line)

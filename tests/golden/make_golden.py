@@ -2,7 +2,9 @@
 
 Run in a container that has the reference checked out (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference/src
+    python tests/golden/make_golden.py --reference <reference checkout>/src
+
+(or set ADAATTN_REFERENCE_SRC to that directory).
 
 It imports the reference's ``AdaAttention`` (``adaattn.attention.adaattn`` is
 imported first: importing ``adaattn.kernels`` first trips a circular import in
@@ -15,7 +17,12 @@ sizes, and stores what the reference computes:
   a strided subset of query rows (rows are independent given K and V);
 * one module-level ``forward`` with its state dict;
 * known answers: a constant query (uniform attention) and the randomized SVD
-  of a rank-2 matrix (the reference's own test_low_rank.py case).
+  of a rank-2 matrix (the reference's own test_low_rank.py case);
+* the kernel-level functions of ``adaattn.kernels`` (flash and adaptive
+  attention on [B, N, H, D]);
+* a small ``AdaptiveTransformer`` from the reference's
+  examples/transformer_integration.py: logits and every block's input and
+  output.
 
 The fixtures are small ``.pt`` files; the GPU box never needs the reference.
 """
@@ -34,6 +41,10 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 from adaattn_b200.workloads import WORKLOADS, make_qkv  # noqa: E402
+
+sys.path.insert(0, os.path.dirname(HERE))
+from golden_util import (TRANSFORMER, kernel_op_inputs, transformer_ids,  # noqa: E402
+                         transformer_state)
 
 ROWS_KEPT = 32
 
@@ -177,21 +188,105 @@ def kat_case(A, LR, out_dir):
     torch.save(rec, os.path.join(out_dir, "kat.pt"))
 
 
+def kernel_ops_case(K, out_dir):
+    """The reference's kernel-level functions (adaattn.kernels) on the seeded
+    [B, N, H, D] inputs of golden_util.kernel_op_inputs. Its native module is
+    never built, so these are the Python paths its callers actually run
+    (kernels/__init__.py:81-213); the entropy helpers exist only in the native
+    module (bindings.cpp:101-135), which the oracle restates and the known
+    answers of the tests pin."""
+    rec = {}
+    for name, (q, k, v) in kernel_op_inputs().items():
+        with torch.no_grad():
+            rec[f"flash_{name}"] = {
+                "out": K.flash_attention_forward(q, k, v, None, False),
+                "out_causal": K.flash_attention_forward(q, k, v, 0.2, True)}
+            rec[f"adaptive_{name}"] = {
+                "fp16": K.adaptive_attention_forward(q, k, v, None, "fp16", None, True),
+                "bf16": K.adaptive_attention_forward(q, k, v, None, "bf16", None, False),
+                "fp32": K.adaptive_attention_forward(q, k, v, None, "fp32", 0.15, True)}
+    torch.save(rec, os.path.join(out_dir, "kernel_ops.pt"))
+
+
+def transformer_case(A, PM, ex_path, out_dir):
+    """The reference's examples/transformer_integration.py AdaptiveTransformer
+    at a small size (golden_util.TRANSFORMER), eval mode, fp32, with the
+    seeded weights of golden_util.transformer_state. Stores the logits and
+    every block's output and decision; and, as the precision noise floor of
+    each block and of the logits, how far they move when every attention
+    decision's precision is replaced by FP32 (same branch)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("transformer_integration", ex_path)
+    ex = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ex)
+    model = ex.AdaptiveTransformer(**TRANSFORMER).eval()
+    model.load_state_dict(transformer_state(model.state_dict()), strict=False)
+    ids = transformer_ids()
+    blocks = []
+
+    def force_fp32(att):
+        orig = att._analyze_attention_pattern
+
+        def forced(q, k):
+            lo, _, ef = orig(q, k)
+            return lo, PM.FP32, ef
+        att._analyze_attention_pattern = forced
+
+    with torch.no_grad():
+        pos = torch.arange(ids.shape[1]).unsqueeze(0)
+        x = model.token_embedding(ids) + model.position_embedding(pos)
+        for blk in model.blocks:
+            att = blk.attention
+            y = blk(x)
+            low, prec, _ = att._analyze_attention_pattern(
+                *[t.view(x.shape[0], x.shape[1], att.num_heads, -1).transpose(1, 2)
+                  for t in (att.q_proj(x), att.k_proj(x))])
+            force_fp32(att)
+            y32 = blk(x)
+            del att._analyze_attention_pattern
+            blocks.append({"y": y.clone(), "fp32_attention_diff": float((y - y32).abs().max()),
+                           "low_rank": bool(low), "precision": prec.name})
+            x = y
+        logits = model(ids)
+        for blk in model.blocks:
+            force_fp32(blk.attention)
+        logits32 = model(ids)
+    torch.save({"config": dict(TRANSFORMER), "logits": logits,
+                "fp32_attention_diff": float((logits - logits32).abs().max()), "blocks": blocks},
+               os.path.join(out_dir, "transformer_small.pt"))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/src")
+    ap.add_argument("--reference", default=os.environ.get("ADAATTN_REFERENCE_SRC"),
+                    help="the reference's src/ directory (or set ADAATTN_REFERENCE_SRC)")
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="fixture names to regenerate (default: all)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or ADAATTN_REFERENCE_SRC) is required")
     sys.path.insert(0, args.reference)
     import adaattn.attention.adaattn as A  # noqa: E402  (must come first)
     from adaattn.attention.base import PrecisionMode as PM  # noqa: E402
     import adaattn.linalg.low_rank as LR  # noqa: E402
+    import adaattn.kernels as K  # noqa: E402
     torch.set_num_threads(os.cpu_count() or 1)
+    want = (lambda n: args.only is None or n in args.only)
     for case in CASES:
-        rec = run_case(A, PM, *case, out_dir=args.out)
-        print(case[0], rec["global"], flush=True)
-    module_case(A, args.out)
-    kat_case(A, LR, args.out)
+        if want(case[0]):
+            rec = run_case(A, PM, *case, out_dir=args.out)
+            print(case[0], rec["global"], flush=True)
+    if want("module_forward"):
+        module_case(A, args.out)
+    if want("kat"):
+        kat_case(A, LR, args.out)
+    if want("kernel_ops"):
+        kernel_ops_case(K, args.out)
+    if want("transformer_small"):
+        ex_path = os.path.join(os.path.dirname(os.path.abspath(args.reference)), "examples",
+                               "transformer_integration.py")
+        transformer_case(A, PM, ex_path, args.out)
 
 
 if __name__ == "__main__":

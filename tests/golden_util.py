@@ -63,3 +63,56 @@ def module_kwargs(rec: dict) -> dict:
         else:
             out[k] = v
     return out
+
+
+# ---------------------------------------------------------------------------
+# Seeded inputs of the kernel-op and transformer fixtures (the fixtures store
+# only the reference's outputs; both sides regenerate the inputs from here).
+# ---------------------------------------------------------------------------
+KERNEL_OP_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+
+
+def kernel_op_inputs() -> dict:
+    """{dtype name: (q, k, v)} [B=1, N=150, H=2, D=64] (two 128-row tiles, the
+    second ragged), drawn in a fixed order."""
+    g = torch.Generator().manual_seed(21)
+    out = {}
+    for dtype in KERNEL_OP_DTYPES:
+        q = (torch.randn(1, 150, 2, 64, generator=g) * 0.5).to(dtype)
+        k = (torch.randn(1, 150, 2, 64, generator=g) * 0.5).to(dtype)
+        v = torch.randn(1, 150, 2, 64, generator=g).to(dtype)
+        out[str(dtype).replace("torch.", "")] = (q, k, v)
+    return out
+
+
+TRANSFORMER = dict(vocab_size=500, embed_dim=128, num_heads=2, num_layers=2, ff_dim=256,
+                   max_seq_len=64)
+
+
+def transformer_state(template: dict, seed: int = 77) -> dict:
+    """Weights for the small AdaptiveTransformer as the GPT-2-small workload
+    initialises them: every Linear / Embedding weight N(0, 0.02), biases 0,
+    LayerNorm weight 1 and bias 0; buffers (call counters) are left alone.
+    ``template`` is a state dict giving the names and shapes; values are
+    drawn in sorted-name order, so any module with these names gets the
+    same weights. The output head is tied to the token embedding, so
+    ``head.weight`` is left out (loading it would overwrite the embedding)."""
+    g = torch.Generator().manual_seed(seed)
+    out = {}
+    for name in sorted(template):
+        t = template[name]
+        if name == "head.weight" or not t.is_floating_point() or name.split(".")[-1].startswith("_"):
+            continue
+        if "norm" in name:
+            val = torch.ones(t.shape) if name.endswith("weight") else torch.zeros(t.shape)
+        elif name.endswith("bias"):
+            val = torch.zeros(t.shape)
+        else:
+            val = torch.randn(t.shape, generator=g) * 0.02
+        out[name] = val
+    return out
+
+
+def transformer_ids(seed: int = 78) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, TRANSFORMER["vocab_size"], (2, TRANSFORMER["max_seq_len"]), generator=g)

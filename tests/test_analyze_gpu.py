@@ -111,3 +111,27 @@ def test_sample_stride_knob(cuda_device):
     t = analyze(q.to(cuda_device), k.to(cuda_device), scale=0.125, sample_stride=8)
     st = O.analyze_per_head(q[:, :, ::8], k[:, :, ::8], cfg, 0.125)
     torch.testing.assert_close(t.head_stats.cpu().double()[..., 0], st["ne"], rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("d", [192, 256])
+def test_head_statistics_wide_heads(d, dtype, cuda_device):
+    """Head dims above 128 with a full 64-row sample: the 16-byte load path
+    needs more than one round of loads per thread (S * D / 8 > 1024 groups)."""
+    g = torch.Generator().manual_seed(13)
+    q = (torch.randn(2, 3, 100, d, generator=g) * 0.7).to(dtype)
+    k = (torch.randn(2, 3, 90, d, generator=g) * 0.7).to(dtype)
+    scale = d ** -0.5
+    cfg = O.OracleConfig()
+    t = _analyze(q, k, cfg, scale, "head", cuda_device)
+    hs = t.head_stats.cpu().double()
+    st = O.analyze_per_head(q, k, cfg, scale)
+    u = _ulp(dtype)
+    torch.testing.assert_close(hs[..., 0], st["ne"], rtol=0, atol=2 * u + 1e-6)
+    torch.testing.assert_close(hs[..., 1], st["max_score"], rtol=2 * u + 1e-6, atol=1e-6)
+    torch.testing.assert_close(hs[..., 2], st["max_prob"], rtol=2 * u + 1e-6, atol=1e-6)
+    # a strided view (not 16-byte rows) takes the scalar path: same statistics
+    qs = torch.zeros(2, 3, 100, d + 1, dtype=dtype, device=cuda_device)[..., :d]
+    qs.copy_(q.to(cuda_device))
+    t2 = _analyze(qs, k, cfg, scale, "head", cuda_device)
+    torch.testing.assert_close(t2.head_stats.cpu(), t.head_stats.cpu(), rtol=0, atol=0)

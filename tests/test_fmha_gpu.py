@@ -13,7 +13,7 @@ import torch
 
 import oracle as O
 from adaattn_b200 import PrecisionMode, attention_forward
-from parity import check_head
+from parity import check_head, half_spacing, record
 
 pytestmark = pytest.mark.gpu
 
@@ -292,9 +292,14 @@ def test_long_sequence_rows_against_torch_fp32(prec, cuda_device):
                 kj = torch.arange(n, device=cuda_device)[None, :]
                 s = s.masked_fill(kj > qi, float("-inf"))
             ref = torch.softmax(s, -1) @ v.float()
-            err = (out[:, :, rows].float() - ref).abs().max().item()
-            m = max(1.0, ref.abs().max().item())
-            # bf16 outputs: one unit in the last place (2^-8 relative); FP32 heads
-            # otherwise 1e-5, 16-bit P 2e-3 more
-            bar = (2 ** -8 + 1e-5) * m if prec == O.FP32 else (2 ** -7 + 2e-3) * m
-            assert err <= bar, f"prec {prec} causal {causal} rows {r0}: err {err:.3e}"
+            got = out[:, :, rows].float()
+            err = (got - ref).abs().max().item()
+            mag = max(ref.abs().max().item(), got.abs().max().item())
+            m = max(1.0, mag)
+            # the parity bars of tests/parity.py: FP32 1e-5, 16-bit heads 2e-3 (FP16
+            # heads round once more in fp16), plus the final cast to bf16
+            bar = (1e-5 if prec == O.FP32 else 2e-3) * m + half_spacing(torch.bfloat16, mag)
+            if prec == O.FP16:
+                bar += half_spacing(torch.float16, mag)
+            record(f"long/p{prec}/c{int(causal)}/r{r0}", O.PREC_NAMES[prec], err, bar)
+            assert err <= bar, f"prec {prec} causal {causal} rows {r0}: err {err:.3e} > {bar:.3e}"

@@ -15,7 +15,7 @@ import oracle as O
 from adaattn_b200 import AdaAttention, PrecisionMode, analyze, attention_forward
 from adaattn_b200.core import possible_precisions
 from golden_util import CASE_NAMES, PREC_CODE, inputs, load, module_kwargs, oracle_config
-from parity import check_head, output_ulp
+from parity import check_head, half_spacing, record
 
 pytestmark = pytest.mark.gpu
 
@@ -71,11 +71,18 @@ def test_golden_outputs(name, granularity, cuda_device):
                 if p == ref_prec[b][h] and lo == bool(ref_low[b, h]) and p in (O.FP32, O.FP16, O.FP8, O.AUTO):
                     g = golden[sl].float()
                     got = full[:, :, rows].float()
-                    mm = max(1.0, g.abs().max().item())
-                    bar = ((1e-5 if p == O.FP32 else 2e-3) + output_ulp(golden.dtype)) * mm
-                    err = (got - g).abs().max().item() if g.numel() else 0.0
                     both_nan = torch.isnan(g).all() and torch.isnan(got).all()
-                    assert both_nan or err <= bar, f"{label}: {err:.3e} > {bar:.3e} vs reference"
+                    if both_nan:
+                        continue
+                    mag = max(g.abs().max().item(), got.abs().max().item()) if g.numel() else 0.0
+                    mm = max(1.0, mag)
+                    # both sides end in the inputs' dtype (two roundings); FP16-computed
+                    # heads of the reference round once more in fp16 before that
+                    bar = ((1e-5 if p == O.FP32 else 2e-3) * mm + 2 * half_spacing(golden.dtype, mag)
+                           + (0.0 if p == O.FP32 else half_spacing(torch.float16, mag)))
+                    err = (got - g).abs().max().item() if g.numel() else 0.0
+                    record(label + "/vs-reference-rows", O.PREC_NAMES[p], err, bar)
+                    assert err <= bar, f"{label}: {err:.3e} > {bar:.3e} vs reference"
 
 
 @pytest.mark.parametrize("name", ["precision_mix_small_fp8"])

@@ -50,3 +50,43 @@ def test_self_attention_stacked_projection_matches_separate(cuda_device):
         sep2, _ = m(x, x.clone(), x.clone())
         err2 = (fused2.float() - sep2.float()).abs().max().item()
         assert err2 <= 2.0 ** -7 * max(1.0, sep2.float().abs().max().item())
+
+
+def test_small_transformer_matches_reference(cuda_device):
+    """The reference's examples/transformer_integration.py decoder at a small
+    size (fixture made by running the reference, tests/golden/make_golden.py)
+    with this package's AdaAttention in every block, global decisions as the
+    reference makes them, fp32.
+
+    Each block is fed the reference's own input to that block, so the check
+    isolates one block at a time; then the whole model's logits. Bar: twice
+    what replacing the reference's attention precision by FP32 moves the same
+    output (its own precision noise), plus 2e-5 relative for the fp32 GEMMs,
+    LayerNorms and GELU on the GPU against the CPU."""
+    from golden_util import TRANSFORMER, load, transformer_ids, transformer_state
+    rec = load("transformer_small")
+    m = AdaptiveTransformer(**TRANSFORMER, decision_granularity="global")
+    m.load_state_dict(transformer_state(m.state_dict()), strict=False)
+    m = m.to(cuda_device).eval()
+    ids = transformer_ids().to(cuda_device)
+    prec_code = {"FP32": 0, "FP16": 1, "BF16": 2, "FP8": 3, "AUTO": 4}
+    with torch.no_grad():
+        pos = torch.arange(ids.shape[1], device=cuda_device).unsqueeze(0)
+        x = m.token_embedding(ids) + m.position_embedding(pos)
+        for i, (blk, ref) in enumerate(zip(m.blocks, rec["blocks"])):
+            y = blk(x)
+            dec = blk.attention.last_decisions
+            assert int(dec.precision.flatten()[0]) == prec_code[ref["precision"]]
+            assert bool(dec.low_rank.flatten()[0]) == ref["low_rank"]
+            want = ref["y"].to(cuda_device)
+            err = (y - want).abs().max().item()
+            bar = 2 * ref["fp32_attention_diff"] + 2e-5 * want.abs().max().item()
+            print(f"block {i}: {ref['precision']} low_rank={ref['low_rank']} err {err:.3e} bar {bar:.3e}")
+            assert err <= bar, f"block {i}: {err:.3e} > {bar:.3e}"
+            x = want  # the next block gets the reference's input
+        logits = m(ids)
+        want = rec["logits"].to(cuda_device)
+        err = (logits.float() - want).abs().max().item()
+        bar = 2 * rec["fp32_attention_diff"] + 2e-5 * want.abs().max().item()
+        print(f"logits: err {err:.3e} bar {bar:.3e}")
+        assert err <= bar, f"logits: {err:.3e} > {bar:.3e}"

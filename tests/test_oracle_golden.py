@@ -114,3 +114,76 @@ def test_fp8_oracle_error_is_bounded():
     got = O.fp8_dense_attention(q, k, v, 0.125, True)
     err = (got - ref).abs().max().item()
     assert 0 < err < 0.1
+
+
+# --------------------------------------------------------------------------
+# Kernel-level ops (adaattn.kernels / _adaattn_cuda) and the small
+# AdaptiveTransformer of examples/transformer_integration.py.
+# --------------------------------------------------------------------------
+
+def test_kernel_ops_match_reference():
+    from golden_util import kernel_op_inputs
+    rec = load("kernel_ops")
+    for name, (q, k, v) in kernel_op_inputs().items():
+        f = rec[f"flash_{name}"]
+        torch.testing.assert_close(O.kernel_flash_attention_forward(q, k, v), f["out"], rtol=0, atol=0)
+        torch.testing.assert_close(O.kernel_flash_attention_forward(q, k, v, 0.2, True), f["out_causal"],
+                                   rtol=0, atol=0)
+        a = rec[f"adaptive_{name}"]
+        torch.testing.assert_close(O.kernel_adaptive_attention_forward(q, k, v, "fp16", None, True),
+                                   a["fp16"], rtol=0, atol=0)
+        torch.testing.assert_close(O.kernel_adaptive_attention_forward(q, k, v, "bf16", None, False),
+                                   a["bf16"], rtol=0, atol=0)
+        torch.testing.assert_close(O.kernel_adaptive_attention_forward(q, k, v, "fp32", 0.15, True),
+                                   a["fp32"], rtol=0, atol=0)
+
+
+def test_entropy_helpers_known_answers():
+    # tests/unit/test_entropy.py:21-48 (uniform -> log n, one-hot -> ~0)
+    uniform = torch.ones(4, 8, 10) / 10
+    torch.testing.assert_close(O.compute_entropy(uniform), torch.full((4, 8), math.log(10)),
+                               rtol=1e-5, atol=0)
+    peaked = torch.zeros(10)
+    peaked[0] = 1.0
+    assert O.compute_entropy(peaked) < 0.01
+    torch.testing.assert_close(O.estimate_effective_rank(uniform), torch.full((4,), 10.0),
+                               rtol=1e-5, atol=0)
+    eff = torch.tensor([4.0, 10.0, 31.0, 32.0, 100.0])
+    assert O.determine_target_ranks(eff).tolist() == [8, 15, 46, 128, 128]
+
+
+def _transformer_oracle(state, ids, cfg_heads):
+    """The example's forward (examples/transformer_integration.py:47-58,
+    :117-132) with the oracle's AdaAttention in each block (global decisions,
+    as the reference makes them); returns (logits, per-block outputs)."""
+    import torch.nn.functional as F
+    e = state["token_embedding.weight"].shape[1]
+    pos = torch.arange(ids.shape[1])
+    x = F.embedding(ids, state["token_embedding.weight"]) + F.embedding(pos, state["position_embedding.weight"])
+    ys = []
+    i = 0
+    while f"blocks.{i}.norm1.weight" in state:
+        p = f"blocks.{i}."
+        att = {k[len(p) + len("attention."):]: v for k, v in state.items() if k.startswith(p + "attention.")}
+        a, _ = O.module_forward(x, x, x, att, cfg_heads, O.OracleConfig(), "global")
+        x = F.layer_norm(x + a, (e,), state[p + "norm1.weight"], state[p + "norm1.bias"])
+        h = F.linear(x, state[p + "ff.0.weight"], state[p + "ff.0.bias"])
+        h = F.linear(F.gelu(h), state[p + "ff.3.weight"], state[p + "ff.3.bias"])
+        x = F.layer_norm(x + h, (e,), state[p + "norm2.weight"], state[p + "norm2.bias"])
+        ys.append(x)
+        i += 1
+    x = F.layer_norm(x, (e,), state["norm.weight"], state["norm.bias"])
+    return F.linear(x, state["token_embedding.weight"]), ys
+
+
+def test_transformer_oracle_matches_reference():
+    """Pins the oracle's module restatement inside the example decoder."""
+    from golden_util import TRANSFORMER, transformer_ids, transformer_state
+    from adaattn_b200.host_model import AdaptiveTransformer
+    rec = load("transformer_small")
+    template = AdaptiveTransformer(**TRANSFORMER).state_dict()
+    state = transformer_state(template)
+    logits, ys = _transformer_oracle(state, transformer_ids(), TRANSFORMER["num_heads"])
+    for got, blk in zip(ys, rec["blocks"]):
+        torch.testing.assert_close(got, blk["y"], rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(logits, rec["logits"], rtol=1e-6, atol=1e-6)
