@@ -151,6 +151,8 @@ struct PrepLaunch {
     float* split_sk;          // [B,H,nt_k]
     float* split_sv;          // [B,H]
     unsigned int* split_amax_v;  // [B,H] max |v| bits, zeroed before launch_split
+    unsigned int* status;        // device status word (bounded waits record ADA_ERR_TIMEOUT)
+    uint64_t timeout_ns;
 };
 int launch_prep16(const PrepLaunch& L, cudaStream_t stream);
 

@@ -707,6 +707,8 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
     pl.fp8_mask = P.fp8_mask;
     pl.nt_q = P.nt_q;
     pl.nt_k = P.nt_k;
+    pl.status = st;
+    pl.timeout_ns = wait_timeout_ns();
     // Low-rank q/k projection on the tensor cores when the inputs are 16-bit
     // and TMA-readable; the SIMT projection kernels cover every other case.
     const int r_pad = P.low_possible ? pad_width(P.r) : 0;

@@ -56,6 +56,8 @@ constexpr int kSmemBudget = 232448 - 1024 - 512;
 // Split-P scale for fp32 heads: P <= 2^8 under the stale-maximum rule, so
 // P * 2^7 stays inside fp16's range and its low part stays normal longer.
 constexpr float kSplitPScale = 128.f;
+// log2(448): E4M3 P is e4m3(448 * p) with p <= 1 under the exact running maximum.
+constexpr float kLog2E4m3Max = 8.807354922057604f;
 
 template <int ELT, int DQK, int DV>
 struct TcCfg {
@@ -464,6 +466,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             float m_run = -INFINITY;
             float l_run = 0.f;
             for (int j = 0; j < nt; ++j) {
+                // The key tile's scale is loaded before the wait for S, off
+                // the softmax's critical path.
+                float ksc = 1.f;
+                if constexpr (ELT >= 2)
+                    if (L.k_scale != nullptr) ksc = L.k_scale[w.bh * L.nt_k + j];
                 ok = mbar_wait(smem_u32(&bars->s_full[t]), sc & 1u, abort_flag, tmo, status);
                 if (!ok) break;
                 ++sc;
@@ -490,7 +497,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 }
                 float sl2 = scale_log2;
                 if constexpr (ELT >= 2)
-                    if (L.k_scale != nullptr) sl2 *= sq * L.k_scale[w.bh * L.nt_k + j];
+                    if (L.k_scale != nullptr) sl2 *= sq * ksc;
                 const int kv0 = j * 128;
                 const bool edge = (kv0 + 128 > Nk) || (causal && kv0 + 127 > tile_r0);
                 if (edge) {
@@ -541,7 +548,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     if (m_cand > m_run + 8.f) m_new = m_cand;
                 }
                 const float alpha = (m_new == m_run) ? 1.f : fast_exp2(m_run - m_new);
-                const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
+                // E4M3 P is quantised as e4m3(448 * p): the factor 448 rides
+                // in the exponent (2^(x + log2 448)), and l sums 448 * p.
+                const float neg_m = (m_new == -INFINITY) ? 0.f : (ELT == 2 ? kLog2E4m3Max - m_new : -m_new);
                 const uint64_t sl2p = f2_pack(sl2, sl2);
                 const uint64_t nmp = f2_pack(neg_m, neg_m);
                 uint64_t ls0 = f2_pack(0.f, 0.f), ls1 = ls0;
@@ -591,7 +600,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                                 p3 = fast_exp2(p3);
                                 ls0 = f2_add(ls0, f2_pack(p0, p1));
                                 ls1 = f2_add(ls1, f2_pack(p2, p3));
-                                pr[i] = pack_e4m3x4(p0 * 448.f, p1 * 448.f, p2 * 448.f, p3 * 448.f);
+                                pr[i] = pack_e4m3x4(p0, p1, p2, p3);
                             } else {
                                 const int c = chunk * 64 + i * 2;
                                 float p0, p1;
@@ -642,7 +651,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             tc_fence_after();
             // ---- epilogue: O / l, rounded like the reference's result, stored ----
             float post = 1.f / l_run;
-            if constexpr (ELT == 2) post *= L.v_scale[w.bh] * (1.f / 448.f);
+            if constexpr (ELT == 2) post *= L.v_scale[w.bh];  // l_run already carries the factor 448
             if constexpr (C::SPLIT) post *= L.v_scale[w.bh] * (1.f / kSplitPScale);
             const bool row_ok = qrow < L.Nq;
             uint8_t* orow = reinterpret_cast<uint8_t*>(L.out);

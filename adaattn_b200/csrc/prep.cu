@@ -548,25 +548,34 @@ __global__ void __launch_bounds__(kThreads) quant8_kernel(const __grid_constant_
         if (tile >= L.nt_k) return;
         const int64_t row0 = tile * 128;
         const int rows = static_cast<int>((L.Nk - row0) < 128 ? (L.Nk - row0) : 128);
-        const int groups = (D + 7) / 8;
         const int64_t base = b * L.vs[0] + h * L.vs[1];
-        float a = 0.f;
-        for (int i = threadIdx.x; i < rows * groups; i += kThreads) {
-            const int rr = i / groups, g = i - rr * groups;
-            float v[8];
-            load8(L.v, L.in_dtype, base + (row0 + rr) * L.vs[2], L.vs[3], g * 8, D, vec_v != 0, v);
+        // all eight 16-byte loads of a thread in flight before the first use
+        float x[8][8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) a = fmaxf(a, fabsf(v[k]));
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * kThreads;
+            if (i < rows * 16)
+                load8(L.v, L.in_dtype, base + (row0 + (i >> 4)) * L.vs[2], L.vs[3], (i & 15) * 8, D,
+                      vec_v != 0, x[u]);
         }
+        float a = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (threadIdx.x + u * kThreads < rows * 16)
+#pragma unroll
+                for (int k = 0; k < 8; ++k) a = fmaxf(a, fabsf(x[u][k]));
         a = block_max256(a, red);
         if (threadIdx.x == 0) L.amax_v[bh * L.nt_k + tile] = a;
         return;
     }
+    // pass 1: blockIdx.z picks the tensor (0 q, 1 k, 2 v), so the three
+    // tiles of one (b, h, tile) stream in parallel CTAs.
     const int width = low ? static_cast<int>(L.r) : D;
-    for (int which = 0; which < 2; ++which) {
+    const int which = static_cast<int>(blockIdx.z);
+    if (which < 2) {
         const int64_t N = which == 0 ? L.Nq : L.Nk;
         const int64_t nt = which == 0 ? L.nt_q : L.nt_k;
-        if (tile >= nt) continue;
+        if (tile >= nt) return;
         const int64_t row0 = tile * 128;
         const int rows = static_cast<int>((N - row0) < 128 ? (N - row0) : 128);
         const void* src;
@@ -620,7 +629,7 @@ __global__ void __launch_bounds__(kThreads) quant8_kernel(const __grid_constant_
             }
         }
     }
-    if (tile < L.nt_k) {
+    if (which == 2 && tile < L.nt_k) {
         float svv = 0.f;
         for (int64_t t = 0; t < L.nt_k; ++t) svv = fmaxf(svv, L.amax_v[bh * L.nt_k + t]);
         const float sv = svv > 0.f ? svv / 448.f : 1.f;
@@ -630,16 +639,153 @@ __global__ void __launch_bounds__(kThreads) quant8_kernel(const __grid_constant_
         const int64_t base = b * L.vs[0] + h * L.vs[1];
         uint8_t* dst = L.ws8_v + (bh * L.Nk + row0) * 128;
         const float isv = 1.f / sv;
-        for (int i = threadIdx.x; i < rows * 16; i += kThreads) {
-            const int rr = i >> 4, g = i & 15;
-            float y[8];
-            load8(L.v, L.in_dtype, base + (row0 + rr) * L.vs[2], L.vs[3], g * 8, D, vec_v != 0, y);
-            reinterpret_cast<uint2*>(dst + rr * 128)[g] = make_uint2(
-                pack_e4m3x4(div_by(y[0], sv, isv), div_by(y[1], sv, isv), div_by(y[2], sv, isv),
-                            div_by(y[3], sv, isv)),
-                pack_e4m3x4(div_by(y[4], sv, isv), div_by(y[5], sv, isv), div_by(y[6], sv, isv),
-                            div_by(y[7], sv, isv)));
+        float x[8][8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * kThreads;
+            if (i < rows * 16)
+                load8(L.v, L.in_dtype, base + (row0 + (i >> 4)) * L.vs[2], L.vs[3], (i & 15) * 8, D,
+                      vec_v != 0, x[u]);
         }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * kThreads;
+            if (i < rows * 16) {
+                const float* y = x[u];
+                reinterpret_cast<uint2*>(dst + (i >> 4) * 128)[i & 15] = make_uint2(
+                    pack_e4m3x4(div_by(y[0], sv, isv), div_by(y[1], sv, isv), div_by(y[2], sv, isv),
+                                div_by(y[3], sv, isv)),
+                    pack_e4m3x4(div_by(y[4], sv, isv), div_by(y[5], sv, isv), div_by(y[6], sv, isv),
+                                div_by(y[7], sv, isv)));
+            }
+        }
+    }
+}
+
+
+// The same quantisation with each 128-row tile staged in shared memory by
+// bulk async copies (one per row, issued by the row's thread), for 16-bit
+// inputs whose rows are 16-byte aligned. A CTA holds one tile of one tensor
+// (blockIdx.z: 0 q, 1 k, 2 v in pass 1; v in pass 0), so CTAs stay small and
+// many tiles stream from HBM at once. Pass 0: V tile amax; pass 1: q / k tile
+// amax and quantisation, v with the head's scale (max of the V tile amaxes).
+constexpr int kStageThreads = 128;
+
+__global__ void __launch_bounds__(kStageThreads) quant8_stage_kernel(const __grid_constant__ PrepLaunch L,
+                                                                     int pass) {
+    __shared__ __align__(128) uint16_t tile_s[128 * 128];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float red[kStageThreads / 32];
+    __shared__ int abort_flag;
+    const int64_t bh = blockIdx.y;
+    int prec, low;
+    get_decision(L.dec, bh, &prec, &low);
+    if (!((L.fp8_mask >> prec) & 1u)) return;
+    const int which = pass == 0 ? 2 : static_cast<int>(blockIdx.z);
+    const int64_t N = which == 0 ? L.Nq : L.Nk;
+    const int64_t nt = which == 0 ? L.nt_q : L.nt_k;
+    const int64_t tile = blockIdx.x;
+    if (tile >= nt) return;
+    const int64_t b = bh / L.H, h = bh % L.H;
+    const int width = (which < 2 && low) ? static_cast<int>(L.r) : static_cast<int>(L.D);
+    const int64_t row0 = tile * 128;
+    const int rows = static_cast<int>((N - row0) < 128 ? (N - row0) : 128);
+    const uint16_t* src;
+    int64_t rs;
+    if (which < 2 && low) {
+        src = static_cast<const uint16_t*>(which == 0 ? L.ws16_q : L.ws16_k) + (bh * N + row0) * L.ld16_qk;
+        rs = L.ld16_qk;
+    } else {
+        const int64_t* st = which == 0 ? L.qs : (which == 1 ? L.ks : L.vs);
+        src = static_cast<const uint16_t*>(which == 0 ? L.q : (which == 1 ? L.k : L.v)) + b * st[0] +
+              h * st[1] + row0 * st[2];
+        rs = st[2];
+    }
+    const int tid = threadIdx.x;
+    const uint32_t row_bytes = static_cast<uint32_t>(width) * 2u;
+    if (tid == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) mbar_arrive_expect_tx(smem_u32(&bar), row_bytes * static_cast<uint32_t>(rows));
+    __syncthreads();
+    if (tid < rows) bulk_load(smem_u32(tile_s + tid * 128), src + tid * rs, row_bytes, smem_u32(&bar));
+    const bool ok = mbar_wait(smem_u32(&bar), 0, &abort_flag, L.timeout_ns, L.status);
+    // Thread t owns 16-byte chunk (t & 15) of rows t/16, t/16 + 8, ...
+    const int g = tid & 15;
+    const int c0 = g * 8;
+    float a = 0.f;
+    const bool need_amax = pass == 0 || which != 2;  // pass 1 quantises v with the head's scale
+    if (ok && need_amax) {
+        for (int rr = tid >> 4; rr < rows; rr += kStageThreads / 16) {
+            if (c0 < width) {
+                const uint4 w4 = *reinterpret_cast<const uint4*>(tile_s + rr * 128 + c0);
+                const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float x0, x1;
+                    if (L.in_dtype == ADA_BF16) {
+                        x0 = __uint_as_float(ws[k] << 16);
+                        x1 = __uint_as_float(ws[k] & 0xffff0000u);
+                    } else {
+                        unpack_f16x2(ws[k], x0, x1);
+                    }
+                    if (c0 + 2 * k < width) a = fmaxf(a, fabsf(x0));
+                    if (c0 + 2 * k + 1 < width) a = fmaxf(a, fabsf(x1));
+                }
+            }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if ((tid & 31) == 0) red[tid >> 5] = a;
+    __syncthreads();
+    a = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    if (pass == 0) {
+        if (tid == 0) L.amax_v[bh * L.nt_k + tile] = a;
+        return;
+    }
+    float sc;
+    if (which < 2) {
+        sc = a > 0.f ? a / 448.f : 1.f;
+        if (tid == 0) {
+            (which == 0 ? L.amax_q : L.amax_k)[bh * nt + tile] = a;
+            (which == 0 ? L.scale_q : L.scale_k)[bh * nt + tile] = sc;
+        }
+    } else {
+        float svv = 0.f;
+        for (int64_t t = 0; t < L.nt_k; ++t) svv = fmaxf(svv, L.amax_v[bh * L.nt_k + t]);
+        sc = svv > 0.f ? svv / 448.f : 1.f;
+        if (tile == 0 && tid == 0) L.scale_v[bh] = sc;
+    }
+    if (!ok) return;
+    const float isc = 1.f / sc;
+    uint8_t* dst = (which == 0 ? L.ws8_q : (which == 1 ? L.ws8_k : L.ws8_v)) + (bh * N + row0) * 128;
+    for (int rr = tid >> 4; rr < rows; rr += kStageThreads / 16) {
+        float y[8];
+        if (c0 < width) {
+            const uint4 w4 = *reinterpret_cast<const uint4*>(tile_s + rr * 128 + c0);
+            const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (L.in_dtype == ADA_BF16) {
+                    y[2 * k] = __uint_as_float(ws[k] << 16);
+                    y[2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u);
+                } else {
+                    unpack_f16x2(ws[k], y[2 * k], y[2 * k + 1]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (c0 + k >= width) y[k] = 0.f;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) y[k] = 0.f;
+        }
+        reinterpret_cast<uint2*>(dst + rr * 128)[g] = make_uint2(
+            pack_e4m3x4(div_by(y[0], sc, isc), div_by(y[1], sc, isc), div_by(y[2], sc, isc), div_by(y[3], sc, isc)),
+            pack_e4m3x4(div_by(y[4], sc, isc), div_by(y[5], sc, isc), div_by(y[6], sc, isc), div_by(y[7], sc, isc)));
     }
 }
 
@@ -702,9 +848,20 @@ int launch_prep8(const PrepLaunch& L, cudaStream_t stream) {
         };
         const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(L.B * L.H));
         const int vq = vec_ok(L.q, L.qs), vk = vec_ok(L.k, L.ks), vv = vec_ok(L.v, L.vs);
+        // Staged path: 16-bit inputs, rows of whole 16-byte chunks, every row
+        // start 16-byte aligned (the low-rank 16-bit region always is).
+        const bool in16 = L.in_dtype == ADA_F16 || L.in_dtype == ADA_BF16;
+        const bool rows_ok = (L.D % 8) == 0 && L.D <= 128 && vq && vk && vv &&
+                             (L.w_down == nullptr || (L.r % 8) == 0);
+        if (in16 && rows_ok && L.status != nullptr) {
+            quant8_stage_kernel<<<grid, kStageThreads, 0, stream>>>(L, 0);
+            if (cudaGetLastError() != cudaSuccess) return ADA_ERR_LAUNCH;
+            quant8_stage_kernel<<<dim3(grid.x, grid.y, 3), kStageThreads, 0, stream>>>(L, 1);
+            return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
+        }
         quant8_kernel<<<grid, kThreads, 0, stream>>>(L, 0, vq, vk, vv);
         if (cudaGetLastError() != cudaSuccess) return ADA_ERR_LAUNCH;
-        quant8_kernel<<<grid, kThreads, 0, stream>>>(L, 1, vq, vk, vv);
+        quant8_kernel<<<dim3(grid.x, grid.y, 3), kThreads, 0, stream>>>(L, 1, vq, vk, vv);
         return cudaGetLastError() == cudaSuccess ? ADA_OK : ADA_ERR_LAUNCH;
     }
     const size_t smem = proj_smem(L, L.w_down != nullptr && !L.low_src16);
