@@ -113,6 +113,7 @@ struct PrepLaunch {
     uint32_t tc16_mask;   // precision codes served by the 16-bit kernels
     uint32_t f16_mask;    // ...of which these compute in fp16 (the rest bf16)
     int direct_ok;        // dense heads already in their compute dtype are read in place
+    int mixed16;          // dense FP16 heads of bf16 inputs read q, k in place: only v is cast
     void* ws16_q;
     void* ws16_k;
     void* ws16_v;
@@ -190,7 +191,8 @@ int launch_split(const PrepLaunch& L, cudaStream_t stream);
 // --- tensor-core FMHA (tcgen05) -----------------------------------------------
 struct TcLaunch {
     CUtensorMap tq, tk, tv;
-    int elt;          // 0 f16, 1 bf16, 2 e4m3; FP32 heads (P as fp16 hi + lo, fp16 V): 3 fp16 q/k, 4 bf16 q/k
+    int elt;          // 0 f16, 1 bf16, 2 e4m3; FP32 heads (P as fp16 hi + lo, fp16 V): 3 fp16 q/k, 4 bf16 q/k;
+                      // 5 FP16 heads of bf16 inputs: bf16 q/k in place, fp16 P and V
     int dqk, dv;      // operand widths (64 or 128)
     int64_t B, H, Nq, Nk;
     int dv_out;       // real value width stored

@@ -698,6 +698,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
     pl.tc16_mask = P.tc16_mask;
     pl.f16_mask = P.f16_mask;
     pl.direct_ok = P.direct_ok ? 1 : 0;
+    pl.mixed16 = (P.direct_ok && P.in_dtype == ADA_BF16) ? 1 : 0;
     pl.ld16_qk = P.ld16_qk;
     pl.ld16_v = P.ld16_v;
     pl.dqk_dense = P.dqk_dense;
@@ -853,7 +854,19 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
             L.round_dtype = cd;
             L.sel = HeadSelect{decisions, pm, low};
             const bool direct = !low && cd == P.in_dtype && P.direct_ok;
-            if (direct) {
+            // FP16 heads of bf16 inputs: bf16 q, k in place, v from the cast region
+            const bool mixed = !low && cd == ADA_F16 && P.in_dtype == ADA_BF16 && P.direct_ok;
+            if (mixed) {
+                L.elt = 5;
+                L.dqk = static_cast<int>(P.D);
+                L.dv = P.dv_pad;
+                const CUtensorMapDataType bf = tma_dtype(ADA_BF16);
+                const int64_t lv = P.ld16_v;
+                if ((rc = make_map(&L.tq, q->data, bf, 2, P.D, P.Nq, P.H, P.B, q->stride[2], q->stride[1], q->stride[0])) ||
+                    (rc = make_map(&L.tk, k->data, bf, 2, P.D, P.Nk, P.H, P.B, k->stride[2], k->stride[1], k->stride[0])) ||
+                    (rc = make_map(&L.tv, ws + P.off16v, dt, 2, L.dv, P.Nk, P.H, P.B, lv, P.Nk * lv, P.H * P.Nk * lv)))
+                    return rc;
+            } else if (direct) {
                 L.dqk = static_cast<int>(P.D);
                 L.dv = static_cast<int>(P.D);
                 if ((rc = make_map(&L.tq, q->data, dt, 2, P.D, P.Nq, P.H, P.B, q->stride[2], q->stride[1], q->stride[0])) ||

@@ -90,7 +90,10 @@ struct TcCfg {
     static constexpr int KSTEP_BYTES = MMA_K * EB;        // 32 bytes either way
     static constexpr int P_COLS = BN * EB / 4;            // TMEM columns holding P
     static constexpr uint32_t FMT = (ELT == 1) ? 1u : 0u; // P·V operands: bf16 = 1, f16 = 0, e4m3 = 0
-    static constexpr uint32_t FMT_QK = (ELT == 1 || ELT == 4) ? 1u : 0u;  // Q·Kᵀ operands
+    // ELT 5: FP16 heads of bf16 inputs. Q·Kᵀ reads the bf16 q, k in place (a
+    // bf16 value in fp16's normal range is exactly its fp16 cast, and every
+    // product is exact in the fp32 accumulator); P and V (cast) are fp16.
+    static constexpr uint32_t FMT_QK = (ELT == 1 || ELT == 4 || ELT == 5) ? 1u : 0u;  // Q·Kᵀ operands
     static constexpr uint32_t IDESC_QK = make_idesc(FMT_QK, FMT_QK, 0, 0, 128, BN);
     static constexpr uint32_t IDESC_PV = make_idesc(FMT, FMT, 0, 1, 128, DV);
     static constexpr int SMEM_BYTES = 2 * QBUF_BYTES + NSTAGE * STAGE_BYTES + 1024 + 512;
@@ -461,7 +464,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             const int qrow = tile_r0 + row;
             const int Nk = static_cast<int>(L.Nk);
             float sq = 1.f;
-            if constexpr (ELT >= 2)
+            if constexpr (ELT >= 2 && ELT <= 4)
                 if (L.q_scale != nullptr) sq = L.q_scale[w.bh * L.nt_q + (w.qtp * 2 + t)];
             float m_run = -INFINITY;
             float l_run = 0.f;
@@ -469,7 +472,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 // The key tile's scale is loaded before the wait for S, off
                 // the softmax's critical path.
                 float ksc = 1.f;
-                if constexpr (ELT >= 2)
+                if constexpr (ELT >= 2 && ELT <= 4)
                     if (L.k_scale != nullptr) ksc = L.k_scale[w.bh * L.nt_k + j];
                 ok = mbar_wait(smem_u32(&bars->s_full[t]), sc & 1u, abort_flag, tmo, status);
                 if (!ok) break;
@@ -496,7 +499,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                     }
                 }
                 float sl2 = scale_log2;
-                if constexpr (ELT >= 2)
+                if constexpr (ELT >= 2 && ELT <= 4)
                     if (L.k_scale != nullptr) sl2 *= sq * ksc;
                 const int kv0 = j * 128;
                 const bool edge = (kv0 + 128 > Nk) || (causal && kv0 + 127 > tile_r0);
@@ -810,6 +813,12 @@ int launch_fmha_tc(const TcLaunch& L, cudaStream_t stream) {
     if (L.elt == 4) {
         if (L.dqk == 128 && L.dv == 128) return launch_variant<4, 128, 128>(L, stream);
         if (L.dqk == 64 && L.dv == 128) return launch_variant<4, 64, 128>(L, stream);
+        return ADA_ERR_UNSUPPORTED;
+    }
+    if (L.elt == 5) {
+        if (L.dqk == 128 && L.dv == 128) return launch_variant<5, 128, 128>(L, stream);
+        if (L.dqk == 64 && L.dv == 128) return launch_variant<5, 64, 128>(L, stream);
+        if (L.dqk == 64 && L.dv == 64) return launch_variant<5, 64, 64>(L, stream);
         return ADA_ERR_UNSUPPORTED;
     }
     if (L.elt == 2) {

@@ -191,7 +191,8 @@ __global__ void __launch_bounds__(kThreads) cast16_kernel(const __grid_constant_
     const int64_t b = bh / L.H, h = bh % L.H;
     const int D = static_cast<int>(L.D);
     const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
-    if (!(low && skip_low_rank_qk)) {
+    const bool qk_in_place = !low && L.mixed16 && cd == ADA_F16 && L.in_dtype == ADA_BF16;
+    if (!(low && skip_low_rank_qk) && !qk_in_place) {
         if (row0 < L.Nq)
             cast_rows(L.q, L.in_dtype, L.qs, b, h, row0, L.Nq, D,
                       reinterpret_cast<uint16_t*>(L.ws16_q) + bh * L.Nq * L.ld16_qk, L.ld16_qk, L.dqk_dense, cd,
