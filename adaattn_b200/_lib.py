@@ -80,6 +80,9 @@ _SIGNATURES = {
     "ada_determine_target_ranks": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_double,
                                              c_void_p, c_void_p]),
     "ada_debug_bounded_wait": (c_int32, [c_uint64, c_void_p]),
+    "ada_attn_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "ada_attn_bwd": (c_int32, [_T, _T, _T, _T, _T, _T, c_void_p, c_int32, POINTER(AdaFwdParams),
+                               _T, _T, _T, c_void_p, c_size_t, c_void_p]),
     "ada_rsvd_workspace_bytes": (c_size_t, [_T, _T, c_int32]),
     "ada_rsvd": (c_int32, [_T, _T, c_int32, c_int32, _T, _T, _T, c_void_p, c_size_t, c_void_p]),
 }

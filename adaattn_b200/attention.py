@@ -33,18 +33,49 @@ from .config import (AttentionConfig, MemoryError, NumericalError, PrecisionMode
 logger = logging.getLogger(__name__)
 
 
-class _ForwardOnly(torch.autograd.Function):
-    """Marks the fused forward as not differentiable through the kernels."""
+class _AttentionGrad(torch.autograd.Function):
+    """Autograd for the fused attention core (the reference gets its
+    gradients from ATen, tests/unit/test_adaattn_unified.py:146-159).
+
+    The forward has already run (the fused kernels wrote ``merged``); this
+    node only records what the backward needs. Its backward calls
+    ``ada_attn_bwd`` per branch: dense heads on q, k; low-rank heads on
+    q_low = q Wᵀ, k_low = k Wᵀ (recomputed in the inputs' dtype, as the
+    forward projects them), then chains W: dq += dq_low W, dW = Σ dq_lowᵀ q +
+    dk_lowᵀ k. Gradients are those of softmax(q kᵀ·scale + mask) v evaluated
+    in fp32 at the operands' values, whatever precision the head's forward
+    used.
+    """
 
     @staticmethod
-    def forward(ctx, out, *inputs):
-        return out
+    def forward(ctx, merged, q, k, v, w_down, table, mask, scale, causal, low_possible):
+        ctx.save_for_backward(merged, q, k, v, w_down)
+        ctx.table, ctx.mask, ctx.scale, ctx.causal = table, mask, scale, causal
+        ctx.low_possible = low_possible
+        return merged
 
     @staticmethod
     def backward(ctx, grad):
-        raise NotImplementedError(
-            "adaattn_b200 implements the attention forward pass only; the fused "
-            "kernels have no backward")
+        merged, q, k, v, w_down = ctx.saved_tensors
+        out = merged.transpose(1, 2)
+        dout = grad.transpose(1, 2)
+        table, mask = ctx.table, ctx.mask
+        kw = dict(scale=ctx.scale, causal=ctx.causal, table=table, attention_mask=mask)
+        dq, dk, dv = core.attention_backward(q, k, v, out, dout, low_rank=False, **kw)
+        dw = None
+        if table is not None and ctx.low_possible and w_down is not None:
+            q_low = nn.functional.linear(q, w_down.to(q.dtype))
+            k_low = nn.functional.linear(k, w_down.to(k.dtype))
+            dql, dkl, dvl = core.attention_backward(q_low, k_low, v, out, dout, low_rank=True, **kw)
+            wf = w_down.float()
+            dq = dq + torch.matmul(dql, wf)
+            dk = dk + torch.matmul(dkl, wf)
+            dv = dv + dvl
+            if ctx.needs_input_grad[4]:
+                dw = (torch.einsum("bhnr,bhnd->rd", dql, q.float())
+                      + torch.einsum("bhnr,bhnd->rd", dkl, k.float())).to(w_down.dtype)
+        return (None, dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dw, None, None, None, None,
+                None)
 
 
 class AdaAttention(nn.Module):
@@ -223,8 +254,12 @@ class AdaAttention(nn.Module):
             v = self.v_proj(value).view(b, nk, h, d).transpose(1, 2)
         merged = torch.empty(b, nq, h, d, dtype=q.dtype, device=q.device)
         attn_out, _ = self.attention_core(q, k, v, attention_mask, out=merged.transpose(1, 2))
-        if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
-            merged = _ForwardOnly.apply(merged, q, k, v)
+        w_down = self.rank_proj_down.weight if self.rank_proj_down is not None else None
+        if torch.is_grad_enabled() and (any(t.requires_grad for t in (q, k, v))
+                                        or (w_down is not None and w_down.requires_grad)):
+            merged = _AttentionGrad.apply(merged, q, k, v, w_down, self.last_decisions,
+                                          attention_mask, self.scale, self.causal,
+                                          self.enable_adaptive_rank)
         output = self.resid_dropout(self.out_proj(merged.view(b, nq, self.embed_dim)))
         return output, None
 

@@ -190,6 +190,44 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scal
     return out
 
 
+def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                       dout: torch.Tensor, *, scale: float, causal: bool = False,
+                       table: Optional[DecisionTable] = None, low_rank: bool = False,
+                       attention_mask: Optional[torch.Tensor] = None):
+    """Gradients (dq, dk, dv) of out = softmax(q kᵀ·scale + mask) v on
+    [B, H, N, D] views, fp32 arithmetic at the operands' values
+    (``ada_attn_bwd``); returned as contiguous fp32 tensors.
+
+    With ``table`` only the heads whose low-rank flag equals ``low_rank`` are
+    computed (the others' gradients stay zero): dense heads pass q, k; low-rank
+    heads pass q_low, k_low and chain ``rank_proj_down`` themselves.
+    """
+    _require_cuda(q, k, v, out, dout)
+    lib = _lib.load()
+    b, h, nq, dqk = q.shape
+    nk, dv_ = k.shape[2], v.shape[3]
+    dev = q.device
+    dq = torch.zeros(b, h, nq, dqk, dtype=torch.float32, device=dev)
+    dk = torch.zeros(b, h, nk, dqk, dtype=torch.float32, device=dev)
+    dv = torch.zeros(b, h, nk, dv_, dtype=torch.float32, device=dev)
+    if b * h == 0 or nq == 0 or nk == 0:
+        return dq, dk, dv
+    mask4 = expand_mask(attention_mask, b, h, nq, nk)
+    p = _lib.AdaFwdParams()
+    p.scale = float(scale)
+    p.causal = int(bool(causal))
+    ws = torch.empty(max(int(lib.ada_attn_bwd_workspace_bytes(b, h, nq)), 1), dtype=torch.uint8, device=dev)
+    tm = _lib.tensor(mask4) if mask4 is not None else None
+    dec = table.decisions.data_ptr() if table is not None else None
+    with torch.cuda.device(dev):
+        rc = lib.ada_attn_bwd(_lib.tensor(q), _lib.tensor(k), _lib.tensor(v), _lib.tensor(out),
+                              _lib.tensor(dout), tm, dec, int(bool(low_rank)), p, _lib.tensor(dq),
+                              _lib.tensor(dk), _lib.tensor(dv), ws.data_ptr(), ws.numel(),
+                              _lib.stream_ptr(dev))
+    _lib.check(rc, "ada_attn_bwd")
+    return dq, dk, dv
+
+
 def _host_params(scale, causal, static_precision, static_low_rank, fp8_mode):
     p = _lib.AdaFwdParams()
     p.scale = float(scale)

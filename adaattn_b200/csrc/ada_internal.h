@@ -236,4 +236,27 @@ struct SimtLaunch {
 };
 int launch_fmha_simt(const SimtLaunch& L, cudaStream_t stream);
 
+// --- attention backward (fp32 CUDA cores) --------------------------------------
+struct BwdLaunch {
+    const void* q;     // [B,H,Nq,dqk] (q or q_low)
+    const void* k;     // [B,H,Nk,dqk]
+    const void* v;     // [B,H,Nk,dv]
+    const void* out;   // [B,H,Nq,dv] forward output
+    const void* dout;  // [B,H,Nq,dv] gradient of the output
+    int q_dtype, k_dtype, v_dtype, out_dtype, dout_dtype;
+    int64_t qs[4], ks[4], vs[4], os[4], gs[4];
+    int64_t B, H, Nq, Nk;
+    int dqk, dv;
+    float scale;
+    int causal;
+    MaskView mask;
+    HeadSelect sel;
+    float* lse;     // [B*H*Nq] workspace
+    float* delta;   // [B*H*Nq] workspace
+    float* dq;      // [B*H][Nq][dqk], zeroed by the caller (atomic accumulation)
+    float* dk;      // [B*H][Nk][dqk]
+    float* dv_out;  // [B*H][Nk][dv]
+};
+int launch_attn_bwd(const BwdLaunch& L, cudaStream_t stream);
+
 }  // namespace ada

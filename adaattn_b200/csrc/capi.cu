@@ -1173,6 +1173,93 @@ int ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v
     return ck(cudaStreamWaitEvent(caller, hp->out[last], 0), "stream wait");
 }
 
+size_t ada_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t nq) {
+    if (batch < 0 || heads < 0 || nq < 0) return 0;
+    return 2 * align256(static_cast<size_t>(batch) * static_cast<size_t>(heads) * static_cast<size_t>(nq) *
+                        sizeof(float));
+}
+
+int ada_attn_bwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const AdaTensor* out,
+                 const AdaTensor* dout, const AdaTensor* mask, const int32_t* decisions, int32_t low_rank,
+                 const AdaFwdParams* params, AdaTensor* dq, AdaTensor* dk, AdaTensor* dv, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if ((rc = check_attn_tensor(q, "q")) || (rc = check_attn_tensor(k, "k")) || (rc = check_attn_tensor(v, "v")) ||
+        (rc = check_attn_tensor(out, "out")) || (rc = check_attn_tensor(dout, "dout")))
+        return rc;
+    if (params == nullptr || dq == nullptr || dk == nullptr || dv == nullptr)
+        return fail(ADA_ERR_INVALID, "null argument");
+    const int64_t B = q->shape[0], H = q->shape[1], Nq = q->shape[2], Dqk = q->shape[3];
+    const int64_t Nk = k->shape[2], Dv = v->shape[3];
+    const AdaTensor* bh_views[4] = {k, v, out, dout};
+    for (const AdaTensor* t : bh_views)
+        if (t->shape[0] != B || t->shape[1] != H) return fail(ADA_ERR_SHAPE, "batch/head extents differ");
+    if (k->shape[3] != Dqk || v->shape[2] != Nk) return fail(ADA_ERR_SHAPE, "k must be [B,H,Nk,Dqk], v [B,H,Nk,Dv]");
+    if (out->shape[2] != Nq || out->shape[3] != Dv || dout->shape[2] != Nq || dout->shape[3] != Dv)
+        return fail(ADA_ERR_SHAPE, "out and dout must be [B,H,Nq,Dv]");
+    if (Dqk < 1 || Dqk > 128 || Dv < 1 || Dv > 128)
+        return fail(ADA_ERR_UNSUPPORTED, "backward head dims must lie in [1, 128]");
+    // gradients: fp32, contiguous [B,H,N,D]
+    auto grad_ok = [](const AdaTensor* g, int64_t b, int64_t h, int64_t n, int64_t d) {
+        if (g->data == nullptr || g->dtype != ADA_F32 || g->ndim != 4) return false;
+        const int64_t want[4] = {b, h, n, d};
+        const int64_t stride[4] = {h * n * d, n * d, d, 1};
+        for (int i = 0; i < 4; ++i) {
+            if (g->shape[i] != want[i]) return false;
+            if (want[i] > 1 && g->stride[i] != stride[i]) return false;
+        }
+        return true;
+    };
+    if (!grad_ok(dq, B, H, Nq, Dqk) || !grad_ok(dk, B, H, Nk, Dqk) || !grad_ok(dv, B, H, Nk, Dv))
+        return fail(ADA_ERR_LAYOUT, "dq, dk, dv must be contiguous fp32 [B,H,N,D] tensors");
+    if (mask != nullptr && mask->data != nullptr) {
+        if (mask->ndim != 4) return fail(ADA_ERR_SHAPE, "mask must be a 4-D [B,H,Nq,Nk] view");
+        if (mask->dtype != ADA_BOOL && !is_float(mask->dtype)) return fail(ADA_ERR_DTYPE, "mask dtype");
+        const int64_t want[4] = {B, H, Nq, Nk};
+        for (int i = 0; i < 4; ++i)
+            if (mask->shape[i] != want[i] && mask->shape[i] != 1) return fail(ADA_ERR_SHAPE, "mask extents");
+    }
+    if (B * H == 0 || Nq == 0 || Nk == 0) return ADA_OK;
+    if (workspace == nullptr || workspace_bytes < ada_attn_bwd_workspace_bytes(B, H, Nq))
+        return fail(ADA_ERR_WORKSPACE, "backward workspace too small");
+    BwdLaunch L{};
+    L.q = q->data;
+    L.k = k->data;
+    L.v = v->data;
+    L.out = out->data;
+    L.dout = dout->data;
+    L.q_dtype = q->dtype;
+    L.k_dtype = k->dtype;
+    L.v_dtype = v->dtype;
+    L.out_dtype = out->dtype;
+    L.dout_dtype = dout->dtype;
+    copy_strides(L.qs, q);
+    copy_strides(L.ks, k);
+    copy_strides(L.vs, v);
+    copy_strides(L.os, out);
+    copy_strides(L.gs, dout);
+    L.B = B;
+    L.H = H;
+    L.Nq = Nq;
+    L.Nk = Nk;
+    L.dqk = static_cast<int>(Dqk);
+    L.dv = static_cast<int>(Dv);
+    L.scale = params->scale;
+    L.causal = params->causal;
+    L.mask = mask_view(mask);
+    L.sel = HeadSelect{decisions, 0x1Fu, low_rank};
+    const size_t half = ada_attn_bwd_workspace_bytes(B, H, Nq) / 2;
+    L.lse = static_cast<float*>(workspace);
+    L.delta = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + half);
+    L.dq = static_cast<float*>(dq->data);
+    L.dk = static_cast<float*>(dk->data);
+    L.dv_out = static_cast<float*>(dv->data);
+    rc = launch_attn_bwd(L, static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "backward launch failed: %s", cudaGetErrorString(cudaGetLastError())) : ADA_OK;
+}
+
 int ada_debug_bounded_wait(uint64_t timeout_ns, void* stream) {
     unsigned int* st;
     int rc = device_setup(&st);

@@ -195,6 +195,24 @@ int         ada_attn_fwd_host(const AdaTensor* q, const AdaTensor* k, const AdaT
                               AdaTensor* out, int64_t chunk_slices, void* device_buffer,
                               size_t buffer_bytes, void* stream);
 
+/* Gradients of the attention core for autograd (the reference's
+ * AdaAttention is differentiable through ATen, tests/unit/
+ * test_adaattn_unified.py:146-159): for every selected head, with
+ * out = softmax(q k^T * scale + mask) v evaluated in fp32 at the operands'
+ * values, writes dq [B,H,Nq,Dqk], dk [B,H,Nk,Dqk] and dv [B,H,Nk,Dv]
+ * (contiguous fp32; dq must be zeroed by the caller, it is accumulated).
+ * Low-rank heads pass q_low, k_low as q, k (Dqk = r) and chain the
+ * projection themselves. decisions: the forward's table, selecting the
+ * heads whose low-rank flag equals low_rank (NULL: every head). Uses
+ * params->scale and ->causal; mask as in ada_attn_fwd. Dqk, Dv <= 128.
+ * Workspace: ada_attn_bwd_workspace_bytes(B, H, Nq) bytes. */
+size_t      ada_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t nq);
+int         ada_attn_bwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v,
+                         const AdaTensor* out, const AdaTensor* dout, const AdaTensor* mask,
+                         const int32_t* decisions, int32_t low_rank, const AdaFwdParams* params,
+                         AdaTensor* dq, AdaTensor* dk, AdaTensor* dv,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* _adaattn_cuda.flash_attention_forward (bindings.cpp:21-68): q, k, v, out are
  * [B, N, H, D] fp16/bf16 (or f32); scale <= 0 means 1/sqrt(D). */
 int         ada_flash_attention_forward(const AdaTensor* q, const AdaTensor* k,

@@ -37,6 +37,7 @@ __all__ = [
     "rsvd_sketch", "E4M3_MAX", "FP8_TILE",
     "kernel_flash_attention_forward", "kernel_adaptive_attention_forward",
     "compute_entropy", "estimate_effective_rank", "determine_target_ranks",
+    "attention_grads", "attention_grads_from_out",
 ]
 
 FP32, FP16, BF16, FP8, AUTO = 0, 1, 2, 3, 4
@@ -513,3 +514,67 @@ def determine_target_ranks(effective_rank: torch.Tensor, min_rank: int = 8,
     return torch.where(effective_rank < threshold,
                        (effective_rank * 1.5).clamp(min_rank, max_rank).to(torch.int64),
                        torch.full_like(effective_rank, max_rank).to(torch.int64))
+
+
+# --------------------------------------------------------------------------
+# Gradients (the reference differentiates through ATen autograd,
+# tests/unit/test_adaattn_unified.py:146-159).
+# --------------------------------------------------------------------------
+
+def attention_grads_from_out(q, k, v, out, dout, scale: float, causal: bool,
+                             attention_mask=None, w_down=None):
+    """The attention backward in float64 by its standard formulas, with the
+    row term Delta = sum(dO * out) taken from the given forward output (as
+    a backward that does not store probabilities computes it):
+    P = softmax(z), dV = Pᵀ dO, dS = P (dO Vᵀ - Delta), dQ = scale dS K,
+    dK = scale dSᵀ Q; with w_down, Q, K are the projections (rounded in
+    their dtype) and dq = dq_low W, dW = dq_lowᵀ q + dk_lowᵀ k.
+    Returns (dq, dk, dv, dw or None) in float64."""
+    if w_down is not None:
+        qa = F.linear(q, w_down.to(q.dtype)).double()
+        ka = F.linear(k, w_down.to(k.dtype)).double()
+    else:
+        qa, ka = q.double(), k.double()
+    vd, od, gd = v.double(), out.double(), dout.double()
+    z = apply_masks(torch.matmul(qa, ka.transpose(-2, -1)) * scale, causal, attention_mask, torch.float64)
+    p = torch.softmax(z, dim=-1)
+    dv = torch.matmul(p.transpose(-2, -1), gd)
+    delta = (gd * od).sum(-1, keepdim=True)
+    ds = p * (torch.matmul(gd, vd.transpose(-2, -1)) - delta)
+    dq = torch.matmul(ds, ka) * scale
+    dk = torch.matmul(ds.transpose(-2, -1), qa) * scale
+    dw = None
+    if w_down is not None:
+        wd = w_down.double()
+        dw = torch.einsum("bhnr,bhnd->rd", dq, q.double()) + torch.einsum("bhnr,bhnd->rd", dk, k.double())
+        dq, dk = torch.matmul(dq, wd), torch.matmul(dk, wd)
+    return dq, dk, dv, dw
+
+
+def attention_grads(q, k, v, dout, scale: float, causal: bool, attention_mask=None,
+                    w_down=None):
+    """float64 autograd of out = softmax(q kᵀ·scale + mask) v (top-left causal,
+    bool masks hide keys, float masks are added); with w_down, q and k are
+    first projected in their own dtype (adaattn.py:357-358) and the
+    projection's rounding is passed through as the identity.
+    Returns (dq, dk, dv, dw or None) in float64."""
+    qd = q.detach().double().requires_grad_(True)
+    kd = k.detach().double().requires_grad_(True)
+    vd = v.detach().double().requires_grad_(True)
+    wd = None
+    if w_down is not None:
+        wd = w_down.detach().double().requires_grad_(True)
+        ql = F.linear(q, w_down.to(q.dtype)).double()
+        kl = F.linear(k, w_down.to(k.dtype)).double()
+        # values of the rounded projection, gradients of the exact one
+        qa = F.linear(qd, wd)
+        ka = F.linear(kd, wd)
+        qa = qa + (ql - qa).detach()
+        ka = ka + (kl - ka).detach()
+    else:
+        qa, ka = qd, kd
+    z = torch.matmul(qa, ka.transpose(-2, -1)) * scale
+    z = apply_masks(z, causal, attention_mask, torch.float64)
+    out = torch.matmul(torch.softmax(z, dim=-1), vd)
+    out.backward(dout.double())
+    return qd.grad, kd.grad, vd.grad, (wd.grad if wd is not None else None)
