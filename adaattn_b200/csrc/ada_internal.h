@@ -26,6 +26,8 @@ struct AnalyzeLaunch {
     float* summary;
     double rank_threshold;
     int enable_rank, enable_prec, default_prec, allow_fp8, granularity;
+    unsigned int* status;  // device status word for the bounded wait of the tensor-core sample product
+    uint64_t timeout_ns;
 };
 int launch_analyze(const AnalyzeLaunch& L, cudaStream_t stream);
 int launch_entropy_rows(const void* w, int dtype, int64_t rows, int64_t len, float* out,

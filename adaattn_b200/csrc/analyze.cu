@@ -30,6 +30,92 @@ struct StatsArgs {
     float* head_sum;    // [B*H]  sum over sampled rows of the normalised row entropy
 };
 
+// Per-row softmax, entropy and maxima of the 64 x 64 raw sample scores `ss`
+// ([64][65] in shared memory), then the head's statistics; every thread of
+// the CTA (256) calls it. Scores are rounded the way the reference's ops
+// round them (adaattn.py:256-275).
+__device__ __forceinline__ void sample_stats(const float* ss, const StatsArgs& a, int bh, float* s_rows,
+                                             unsigned int* s_max_score, unsigned int* s_max_prob) {
+    const int tid = threadIdx.x;
+    const int S = a.S;
+    // Thread layout: 4 consecutive lanes own one sample row, 16 columns each.
+    const int r = tid >> 2;
+    const int c0 = (tid & 3) * 16;
+    const bool row_ok = r < S;
+    float sc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) sc[j] = ss[r * (kSample + 1) + c0 + j];
+    // scores = round(round(q k^T) * scale); track max |score|.
+    float local_max_abs = 0.f;
+    float row_max = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const bool ok = row_ok && (c0 + j) < S;
+        float s = round_to(round_to(sc[j], a.dtype) * a.scale, a.dtype);
+        sc[j] = ok ? s : -INFINITY;
+        if (ok) {
+            local_max_abs = fmaxf(local_max_abs, fabsf(s));
+            row_max = fmaxf(row_max, s);
+        }
+    }
+    row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, 1));
+    row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, 2));
+    // softmax in fp32 on the rounded scores, output rounded to the dtype.
+    float e[16];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        e[j] = (sc[j] == -INFINITY) ? 0.f : expf(sc[j] - row_max);
+        sum += e[j];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    const float inv = 1.f / sum;
+    float local_max_prob = 0.f;
+    float ent = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        if (row_ok && (c0 + j) < S) {
+            const float p = round_to(e[j] * inv, a.dtype);
+            local_max_prob = fmaxf(local_max_prob, p);
+            const float t1 = round_to(p + a.eps, a.dtype);
+            const float t2 = round_to(logf(t1), a.dtype);
+            ent += round_to(p * t2, a.dtype);
+        }
+    }
+    ent += __shfl_xor_sync(0xffffffffu, ent, 1);
+    ent += __shfl_xor_sync(0xffffffffu, ent, 2);
+    if (row_ok && (tid & 3) == 0) {
+        const float row_entropy = -round_to(ent, a.dtype);
+        s_rows[r] = round_to(row_entropy / a.log_s, a.dtype);
+    }
+    // block maxima (non-negative floats compare like their bit patterns)
+    for (int o = 16; o > 0; o >>= 1) {
+        local_max_abs = fmaxf(local_max_abs, __shfl_xor_sync(0xffffffffu, local_max_abs, o));
+        local_max_prob = fmaxf(local_max_prob, __shfl_xor_sync(0xffffffffu, local_max_prob, o));
+    }
+    __syncthreads();
+    if ((tid & 31) == 0) {
+        atomicMax(s_max_score, __float_as_uint(local_max_abs));
+        atomicMax(s_max_prob, __float_as_uint(local_max_prob));
+    }
+    __syncthreads();
+    if (tid < 32) {
+        float v = 0.f;
+        for (int i = tid; i < S; i += 32) v += s_rows[i];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (tid == 0) {
+            const float ne = round_to(v / static_cast<float>(S), a.dtype);
+            float* hs = a.head_stats + static_cast<int64_t>(bh) * 4;
+            hs[0] = ne;
+            hs[1] = __uint_as_float(*s_max_score);
+            hs[2] = __uint_as_float(*s_max_prob);
+            hs[3] = ne * static_cast<float>(a.Nq < a.Nk ? a.Nq : a.Nk);
+            a.head_sum[bh] = v;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) analyze_stats_kernel(StatsArgs a) {
     extern __shared__ __align__(16) float sm[];
     const int D = static_cast<int>(a.D);
@@ -144,82 +230,138 @@ __global__ void __launch_bounds__(kThreads) analyze_stats_kernel(StatsArgs a) {
     }
     __syncthreads();
 
-    // Thread layout: 4 consecutive lanes own one sample row, 16 columns each.
-    const int r = tid >> 2;
-    const int c0 = (tid & 3) * 16;
-    const bool row_ok = r < S;
-    float sc[16];
+    sample_stats(ss, a, bh, s_rows, &s_max_score, &s_max_prob);
+}
+
+
+// The same statistics with the 64 x 64 x D sample product on the tensor
+// cores, for 16-bit q, k whose rows are 16-byte aligned and D % 16 == 0
+// (D <= 256). The sample rows are written to shared memory in the 128-byte
+// swizzled K-major layout (q as a 128-row A operand whose rows 64..127 are
+// zero, k as a 64-row B operand); one thread issues D / 16 tcgen05.mma
+// (M = 128, N = 64, fp32 accumulate) into 64 TMEM columns and commits to an
+// mbarrier (bounded wait); warps 0 and 1 then read their 32 rows each and
+// run the per-row softmax and entropy with the reference's roundings, one
+// row per thread. The products are exact and summed in fp32, as in the
+// CUDA-core kernel (the order of the sum differs).
+struct StatsTcArgs {
+    StatsArgs a;
+    unsigned int* status;
+    uint64_t timeout_ns;
+};
+
+__global__ void __launch_bounds__(kThreads) analyze_stats_tc_kernel(const __grid_constant__ StatsTcArgs T) {
+    const StatsArgs& a = T.a;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int D = static_cast<int>(a.D);
+    const int boxes = (D + 63) / 64;
+    uint8_t* sA = base;                        // boxes x [128 rows x 128 B]
+    uint8_t* sB = base + boxes * 128 * 128;    // boxes x [64 rows x 128 B]
+    float* ss = reinterpret_cast<float*>(sA);  // [64][65] raw scores, over A once the product is done
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag;
+    __shared__ unsigned int s_max_score, s_max_prob;
+    __shared__ float s_rows[kSample];
+    const int bh = blockIdx.x;
+    const int b = bh / static_cast<int>(a.H);
+    const int h = bh % static_cast<int>(a.H);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int S = a.S;
+    if (tid == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_flag = 0;
+        s_max_score = 0u;
+        s_max_prob = 0u;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(&tmem_base), 64);
+        tmem_relinquish();
+    }
+    // Sample rows -> swizzled tiles: 16-byte chunk c of row r goes to chunk
+    // (c & 7) ^ (r & 7) of that row's 128-byte line in box c / 8. A thread's
+    // loads (at most 8 per tensor at D = 256) are all in flight before the
+    // first store.
+    const int64_t qbase = b * a.qs[0] + h * a.qs[1];
+    const int64_t kbase = b * a.ks[0] + h * a.ks[1];
+    const int g = D >> 3;  // 16-byte chunks per row
+    const int n = kSample * g;
+    constexpr int kMaxPer = (kSample * 32 + kThreads - 1) / kThreads;  // D <= 256
+    uint4 vq[kMaxPer], vk[kMaxPer];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) sc[j] = ss[r * (kSample + 1) + c0 + j];
-    // scores = round(round(q k^T) * scale); track max |score|.
-    float local_max_abs = 0.f;
-    float row_max = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const bool ok = row_ok && (c0 + j) < S;
-        float s = round_to(round_to(sc[j], a.dtype) * a.scale, a.dtype);
-        sc[j] = ok ? s : -INFINITY;
-        if (ok) {
-            local_max_abs = fmaxf(local_max_abs, fabsf(s));
-            row_max = fmaxf(row_max, s);
+    for (int u = 0; u < kMaxPer; ++u) {
+        const int idx = tid + u * kThreads;
+        vq[u] = make_uint4(0u, 0u, 0u, 0u);
+        vk[u] = vq[u];
+        if (idx < n) {
+            const int r = idx / g, c = idx - r * g;
+            if (r < S) {
+                const int64_t row = static_cast<int64_t>(r) * a.stride;
+                vq[u] = reinterpret_cast<const uint4*>(a.q)[(qbase + row * a.qs[2] + c * 8) / 8];
+                vk[u] = reinterpret_cast<const uint4*>(a.k)[(kbase + row * a.ks[2] + c * 8) / 8];
+            }
         }
     }
-    row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, 1));
-    row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, 2));
-    // softmax in fp32 on the rounded scores, output rounded to the dtype.
-    float e[16];
-    float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        e[j] = (sc[j] == -INFINITY) ? 0.f : expf(sc[j] - row_max);
-        sum += e[j];
-    }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    const float inv = 1.f / sum;
-    float local_max_prob = 0.f;
-    float ent = 0.f;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        if (row_ok && (c0 + j) < S) {
-            const float p = round_to(e[j] * inv, a.dtype);
-            local_max_prob = fmaxf(local_max_prob, p);
-            const float t1 = round_to(p + a.eps, a.dtype);
-            const float t2 = round_to(logf(t1), a.dtype);
-            ent += round_to(p * t2, a.dtype);
+    for (int u = 0; u < kMaxPer; ++u) {
+        const int idx = tid + u * kThreads;
+        if (idx < n) {
+            const int r = idx / g, c = idx - r * g;
+            const int off = r * 128 + (((c & 7) ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(sA + (c >> 3) * (128 * 128) + off) = vq[u];
+            *reinterpret_cast<uint4*>(sB + (c >> 3) * (64 * 128) + off) = vk[u];
         }
     }
-    ent += __shfl_xor_sync(0xffffffffu, ent, 1);
-    ent += __shfl_xor_sync(0xffffffffu, ent, 2);
-    if (row_ok && (tid & 3) == 0) {
-        const float row_entropy = -round_to(ent, a.dtype);
-        s_rows[r] = round_to(row_entropy / a.log_s, a.dtype);
+    // rows 64..127 of the A operand: zero
+    for (int idx = tid; idx < n; idx += kThreads) {
+        const int r = kSample + idx / g, c = idx % g;
+        *reinterpret_cast<uint4*>(sA + (c >> 3) * (128 * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
+            make_uint4(0u, 0u, 0u, 0u);
     }
-    // block maxima (non-negative floats compare like their bit patterns)
-    for (int o = 16; o > 0; o >>= 1) {
-        local_max_abs = fmaxf(local_max_abs, __shfl_xor_sync(0xffffffffu, local_max_abs, o));
-        local_max_prob = fmaxf(local_max_prob, __shfl_xor_sync(0xffffffffu, local_max_prob, o));
-    }
+    fence_proxy_async_smem();
+    tc_fence_before();
     __syncthreads();
-    if ((tid & 31) == 0) {
-        atomicMax(&s_max_score, __float_as_uint(local_max_abs));
-        atomicMax(&s_max_prob, __float_as_uint(local_max_prob));
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    if (tid == 0) {
+        const uint32_t fmt = a.dtype == ADA_BF16 ? 1u : 0u;
+        const uint32_t idesc = make_idesc(fmt, fmt, 0, 0, 128, 64);
+        const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+        for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t box = static_cast<uint32_t>(ks >> 2), inner = static_cast<uint32_t>((ks & 3) * 32);
+            mma_ss_f16(tmem, make_sdesc_sw128(a0 + box * (128 * 128) + inner, 16, 1024),
+                       make_sdesc_sw128(b0 + box * (64 * 128) + inner, 16, 1024), idesc, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&bar));
     }
-    __syncthreads();
-    if (tid < 32) {
-        float v = 0.f;
-        for (int i = tid; i < S; i += 32) v += s_rows[i];
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (tid == 0) {
-            const float ne = round_to(v / static_cast<float>(S), a.dtype);
-            float* hs = a.head_stats + static_cast<int64_t>(bh) * 4;
-            hs[0] = ne;
-            hs[1] = __uint_as_float(s_max_score);
-            hs[2] = __uint_as_float(s_max_prob);
-            hs[3] = ne * static_cast<float>(a.Nq < a.Nk ? a.Nq : a.Nk);
-            a.head_sum[bh] = v;
+    const bool ok = mbar_wait(smem_u32(&bar), 0, &abort_flag, T.timeout_ns, T.status);
+    tc_fence_after();
+    // every MMA has completed (or the wait gave up): A may be overwritten
+    if (warp < 2) {
+        const int r = warp * 32 + lane;  // TMEM lane == sample row
+        uint32_t u0[32], u1[32];
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        tmem_ld32(taddr, u0);
+        tmem_ld32(taddr + 32, u1);
+        tmem_ld_wait();
+        reg_fence32(u0);
+        reg_fence32(u1);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            ss[r * (kSample + 1) + j] = ok ? __uint_as_float(u0[j]) : NAN;
+            ss[r * (kSample + 1) + 32 + j] = ok ? __uint_as_float(u1[j]) : NAN;
         }
     }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 64);
+    }
+    sample_stats(ss, a, bh, s_rows, &s_max_score, &s_max_prob);
 }
 
 struct DecideArgs {
@@ -447,14 +589,28 @@ int launch_analyze(const AnalyzeLaunch& L, cudaStream_t stream) {
         a.vec = (L.dtype == ADA_F16 || L.dtype == ADA_BF16) && (L.D % 8) == 0 && rows16(L.q, L.qs) &&
                 rows16(L.k, L.ks);
     }
-    const size_t smem = static_cast<size_t>(2 * kSample * (((L.D + 3) & ~3) + 4) + kSample * (kSample + 1)) *
-                        sizeof(float);
-    if (smem > 48 * 1024) {
-        if (cudaFuncSetAttribute(analyze_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (a.vec && (L.D % 16) == 0 && L.D <= 256 && L.status != nullptr) {
+        // tensor-core sample product: A 128 rows and B 64 rows per 64-column box
+        const int boxes = static_cast<int>((L.D + 63) / 64);
+        const size_t smem = static_cast<size_t>(boxes) * (128 + 64) * 128 + 1024;
+        if (cudaFuncSetAttribute(analyze_stats_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem)) != cudaSuccess)
             return ADA_ERR_LAUNCH;
+        StatsTcArgs t{};
+        t.a = a;
+        t.status = L.status;
+        t.timeout_ns = L.timeout_ns;
+        analyze_stats_tc_kernel<<<static_cast<unsigned>(L.B * L.H), kThreads, smem, stream>>>(t);
+    } else {
+        const size_t smem = static_cast<size_t>(2 * kSample * (((L.D + 3) & ~3) + 4) + kSample * (kSample + 1)) *
+                            sizeof(float);
+        if (smem > 48 * 1024) {
+            if (cudaFuncSetAttribute(analyze_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)) != cudaSuccess)
+                return ADA_ERR_LAUNCH;
+        }
+        analyze_stats_kernel<<<static_cast<unsigned>(L.B * L.H), kThreads, smem, stream>>>(a);
     }
-    analyze_stats_kernel<<<static_cast<unsigned>(L.B * L.H), kThreads, smem, stream>>>(a);
     if (cudaGetLastError() != cudaSuccess) return ADA_ERR_LAUNCH;
 
     DecideArgs d{};

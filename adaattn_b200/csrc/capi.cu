@@ -493,6 +493,8 @@ int analyze_setup(const AdaTensor* q, const AdaTensor* k, const AdaAnalyzeParams
     L->default_prec = params->default_precision;
     L->allow_fp8 = params->allow_fp8;
     L->granularity = params->granularity;
+    L->status = st;
+    L->timeout_ns = wait_timeout_ns();
     return ADA_OK;
 }
 int device_status_word(unsigned int** status) { return device_setup(status); }
