@@ -83,6 +83,7 @@ _SIGNATURES = {
     "ada_attn_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "ada_attn_bwd": (c_int32, [_T, _T, _T, _T, _T, _T, c_void_p, c_int32, POINTER(AdaFwdParams),
                                _T, _T, _T, c_void_p, c_size_t, c_void_p]),
+    "ada_linear": (c_int32, [_T, _T, _T, _T, c_int32, _T, c_void_p]),
     "ada_rsvd_workspace_bytes": (c_size_t, [_T, _T, c_int32]),
     "ada_rsvd": (c_int32, [_T, _T, c_int32, c_int32, _T, _T, _T, c_void_p, c_size_t, c_void_p]),
 }
@@ -134,21 +135,18 @@ def check(rc: int, what: str) -> None:
     raise KernelError(msg, rc)
 
 
+_I64x4 = c_int64 * 4
+
+
 def tensor(t: torch.Tensor) -> AdaTensor:
     """Describe a torch tensor (up to 4-D) for the C ABI; no copy."""
-    if t.dim() > 4:
-        raise ShapeError(f"at most 4 dimensions, got {t.dim()}")
-    d = AdaTensor()
-    d.data = t.data_ptr() if t.numel() > 0 else 0
-    try:
-        d.dtype = DTYPE_CODE[t.dtype]
-    except KeyError:
-        raise TypeError(f"unsupported dtype {t.dtype}") from None
-    d.ndim = t.dim()
-    for i in range(t.dim()):
-        d.shape[i] = t.shape[i]
-        d.stride[i] = t.stride(i)
-    return d
+    nd = t.dim()
+    if nd > 4:
+        raise ShapeError(f"at most 4 dimensions, got {nd}")
+    code = DTYPE_CODE.get(t.dtype)
+    if code is None:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    return AdaTensor(t.data_ptr() if t.numel() > 0 else 0, code, nd, _I64x4(*t.shape), _I64x4(*t.stride()))
 
 
 def stream_ptr(device: torch.device) -> int:

@@ -236,7 +236,36 @@ class AdaAttention(nn.Module):
         except torch.cuda.OutOfMemoryError as e:
             raise MemoryError(f"GPU out of memory: {e}") from e
 
-    def _forward_impl(self, query, key, value, attention_mask=None, need_weights=False):
+    def forward_with_residual(self, x: Tensor, attention_mask: Optional[Tensor] = None) -> Tensor:
+        """``x + self(x, x, x)[0]`` for self-attention, the residual sum of the
+        host transformer block (examples/transformer_integration.py:47-48)
+        fused into out_proj's epilogue (rounded like the two PyTorch ops:
+        out_proj's result, then the sum). The output dropout must be inactive
+        (eval mode or p = 0)."""
+        if self.training and self.resid_dropout.p > 0:
+            raise RuntimeError("forward_with_residual needs the output dropout inactive (eval() or p=0)")
+        self._validate_inputs(x, x, x, attention_mask)
+        try:
+            output, _ = self._forward_impl(x, x, x, attention_mask, residual=x)
+            self._check_numerical_stability(output, "attention output")
+            return output
+        except torch.cuda.OutOfMemoryError as e:
+            raise MemoryError(f"GPU out of memory: {e}") from e
+
+    @staticmethod
+    def _dense_on_tensor_cores(x: Tensor) -> bool:
+        # The tensor-core layer (core.linear) serves 16-bit CUDA tensors; fp32
+        # layers stay on the reference's own fp32 Linear, whose rounding a
+        # tensor-core product would change.
+        return x.is_cuda and x.dtype in (torch.bfloat16, torch.float16)
+
+    def _linear(self, layer: nn.Linear, x: Tensor, residual: Optional[Tensor] = None) -> Tensor:
+        if self._dense_on_tensor_cores(x):
+            return core.linear(x, layer.weight, layer.bias, residual=residual)
+        y = layer(x)
+        return y if residual is None else residual + y
+
+    def _forward_impl(self, query, key, value, attention_mask=None, need_weights=False, residual=None):
         # adaattn.py:396-460 without the flash_attn branch.
         b, nq, _ = query.shape
         nk = key.shape[1]
@@ -245,13 +274,16 @@ class AdaAttention(nn.Module):
             # Self-attention: one GEMM against the stacked q/k/v weights
             # (same values as the three Linears); q, k, v are column views.
             w, bias = self._stacked_qkv()
-            qkv = torch.nn.functional.linear(query, w, bias)
+            if self._dense_on_tensor_cores(query):
+                qkv = core.linear(query, w, bias)
+            else:
+                qkv = torch.nn.functional.linear(query, w, bias)
             e = self.embed_dim
             q, k, v = (qkv[..., i * e:(i + 1) * e].view(b, nq, h, d).transpose(1, 2) for i in range(3))
         else:
-            q = self.q_proj(query).view(b, nq, h, d).transpose(1, 2)
-            k = self.k_proj(key).view(b, nk, h, d).transpose(1, 2)
-            v = self.v_proj(value).view(b, nk, h, d).transpose(1, 2)
+            q = self._linear(self.q_proj, query).view(b, nq, h, d).transpose(1, 2)
+            k = self._linear(self.k_proj, key).view(b, nk, h, d).transpose(1, 2)
+            v = self._linear(self.v_proj, value).view(b, nk, h, d).transpose(1, 2)
         merged = torch.empty(b, nq, h, d, dtype=q.dtype, device=q.device)
         attn_out, _ = self.attention_core(q, k, v, attention_mask, out=merged.transpose(1, 2))
         w_down = self.rank_proj_down.weight if self.rank_proj_down is not None else None
@@ -260,7 +292,9 @@ class AdaAttention(nn.Module):
             merged = _AttentionGrad.apply(merged, q, k, v, w_down, self.last_decisions,
                                           attention_mask, self.scale, self.causal,
                                           self.enable_adaptive_rank)
-        output = self.resid_dropout(self.out_proj(merged.view(b, nq, self.embed_dim)))
+        if residual is not None:
+            return self._linear(self.out_proj, merged.view(b, nq, self.embed_dim), residual), None
+        output = self.resid_dropout(self._linear(self.out_proj, merged.view(b, nq, self.embed_dim)))
         return output, None
 
     def _stacked_qkv(self) -> Tuple[Tensor, Optional[Tensor]]:

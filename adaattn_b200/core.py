@@ -228,6 +228,117 @@ def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: t
     return dq, dk, dv
 
 
+_ACTIVATIONS = {None: 0, "none": 0, "gelu": 1}
+
+
+def _linear_launch(x2: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
+                   r2: Optional[torch.Tensor], act: int) -> torch.Tensor:
+    """One ada_linear call on 2-D views; y rows padded to 8 elements (16 bytes)
+    and returned as a view of the first N columns."""
+    lib = _lib.load()
+    m, n = x2.shape[0], weight.shape[0]
+    n_pad = (n + 7) // 8 * 8
+    y = torch.empty(m, n_pad, dtype=x2.dtype, device=x2.device)[:, :n]
+    tb = _lib.tensor(bias) if bias is not None else None
+    tr = _lib.tensor(r2) if r2 is not None else None
+    dev = x2.device
+    args = (_lib.tensor(x2), _lib.tensor(weight), tb, tr, act, _lib.tensor(y))
+    if dev.index == torch.cuda.current_device():
+        rc = lib.ada_linear(*args, torch.cuda.current_stream(dev).cuda_stream)
+    else:
+        with torch.cuda.device(dev):
+            rc = lib.ada_linear(*args, torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(rc, "ada_linear")
+    return y
+
+
+def _unflat(y: torch.Tensor, lead) -> torch.Tensor:
+    if len(lead) == 1:
+        return y
+    return y.unflatten(0, lead) if len(lead) else y[0]
+
+
+def _rows(t: torch.Tensor) -> torch.Tensor:
+    """[..., K] as a 2-D [M, K] view with unit column stride and 16-byte
+    aligned rows (a copy only when the layout cannot be read in place)."""
+    t2 = t if t.dim() == 2 else t.reshape(-1, t.shape[-1])
+    if t2.shape[0] > 1 and t2.shape[1] > 1 and (
+            t2.stride(1) != 1 or (t2.stride(0) * t2.element_size()) % 16 or t2.data_ptr() % 16):
+        t2 = t2.contiguous()
+    elif t2.data_ptr() % 16:
+        t2 = t2.clone()
+    return t2
+
+
+class _LinearGrad(torch.autograd.Function):
+    """Gradients of y = act(x Wᵀ + b) + r. The forward runs on ada_linear;
+    the backward is the Linear's own pair of GEMMs (and GELU's derivative at
+    the recomputed pre-activation), in the inputs' dtype like ATen's."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, residual, act):
+        ctx.act = act
+        ctx.has_bias = bias is not None
+        ctx.has_r = residual is not None
+        ctx.save_for_backward(x, weight, bias)
+        x2 = _rows(x)
+        r2 = _rows(residual) if residual is not None else None
+        return _unflat(_linear_launch(x2, weight, bias, r2, act), x.shape[:-1])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, bias = ctx.saved_tensors
+        dh = dy
+        if ctx.act == 1:
+            h = _unflat(_linear_launch(_rows(x), weight, bias, None, 0), x.shape[:-1])
+            hf = h.float()
+            cdf = 0.5 * (1.0 + torch.erf(hf * 0.7071067811865476))
+            pdf = torch.exp(-0.5 * hf * hf) * 0.3989422804014327
+            dh = (dy.float() * (cdf + hf * pdf)).to(dy.dtype)
+        dx = dh.matmul(weight) if ctx.needs_input_grad[0] else None
+        dw = dh.reshape(-1, dh.shape[-1]).t().matmul(x.reshape(-1, x.shape[-1])) \
+            if ctx.needs_input_grad[1] else None
+        db = dh.reshape(-1, dh.shape[-1]).sum(0) if ctx.has_bias and ctx.needs_input_grad[2] else None
+        dr = dy if ctx.has_r and ctx.needs_input_grad[3] else None
+        return dx, dw, db, dr, None
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, *,
+           residual: Optional[torch.Tensor] = None, activation: Optional[str] = None) -> torch.Tensor:
+    """``act(x @ weight.T + bias) + residual`` on the tensor cores (``ada_linear``):
+    the module's q/k/v projections and out_proj (adaattn.py:411-418, :457)
+    and the host block's feed-forward, as one launch each with the bias,
+    the GELU (erf form) and the residual sum fused into the epilogue.
+
+    x [..., K] and weight [N, K] (nn.Linear's layout) are bf16 or fp16 on an
+    sm_100 device; K must be a multiple of 8. The result [..., N] rounds like
+    the PyTorch ops it replaces (Linear, then GELU, then the sum, each in the
+    inputs' dtype); its rows are padded to 16 bytes in memory. Autograd is
+    supported (the backward uses the Linear's own GEMMs).
+    """
+    _require_cuda(x, weight, bias, residual)
+    act = _ACTIVATIONS.get(activation)
+    if act is None:
+        raise ValueError(f"activation must be None or 'gelu', got {activation!r}")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"linear runs in bf16 or fp16, got {x.dtype}")
+    if weight.dtype != x.dtype or (bias is not None and bias.dtype != x.dtype) or (
+            residual is not None and residual.dtype != x.dtype):
+        raise TypeError("x, weight, bias and residual must share one dtype")
+    if x.shape[-1] != weight.shape[1]:
+        raise ShapeError(f"x has {x.shape[-1]} features, weight expects {weight.shape[1]}")
+    if residual is not None and tuple(residual.shape) != tuple(x.shape[:-1]) + (weight.shape[0],):
+        raise ShapeError(f"residual must be {tuple(x.shape[:-1]) + (weight.shape[0],)}, "
+                         f"got {tuple(residual.shape)}")
+    w = weight if (weight.stride(-1) == 1 and (weight.stride(0) * 2) % 16 == 0
+                   and weight.data_ptr() % 16 == 0) else weight.contiguous()
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad
+                                       for t in (x, weight, bias, residual)):
+        return _LinearGrad.apply(x, w, bias, residual, act)
+    y = _linear_launch(_rows(x), w, bias, _rows(residual) if residual is not None else None, act)
+    return _unflat(y, x.shape[:-1])
+
+
 def _host_params(scale, causal, static_precision, static_low_rank, fp8_mode):
     p = _lib.AdaFwdParams()
     p.scale = float(scale)

@@ -238,6 +238,26 @@ struct SimtLaunch {
 };
 int launch_fmha_simt(const SimtLaunch& L, cudaStream_t stream);
 
+// --- dense layers (tcgen05 GEMM with a fused epilogue) --------------------------
+struct LinearLaunch {
+    CUtensorMap tx;      // x [M, K], 64-column x 128-row boxes, 128-byte swizzle
+    CUtensorMap tw;      // W [N, K], 64-column x 256-row boxes
+    CUtensorMap ty;      // y [M, N], 64-column x 32-row boxes (stores), when tma_io
+    CUtensorMap tr;      // resid [M, N], 64-column x 32-row boxes (loads), when tma_io and resid
+    const void* bias;    // [N] or null
+    const void* resid;   // [M, N] rows at ld_r, or null
+    void* y;             // [M, N] rows at ld_y
+    int64_t M, N, K;
+    int64_t ld_y, ld_r;  // row strides in elements
+    int dtype;           // ADA_BF16 or ADA_F16 (x, W, bias, resid and y alike)
+    int act;             // 0: none, 1: GELU (erf form)
+    int vec;             // 16-byte aligned rows of y and resid
+    int tma_io;          // y (and resid) through per-warp shared-memory tiles and TMA
+    unsigned int* status;
+    uint64_t timeout_ns;
+};
+int launch_linear_tc(const LinearLaunch& L, cudaStream_t stream);
+
 // --- attention backward (fp32 CUDA cores) --------------------------------------
 struct BwdLaunch {
     const void* q;     // [B,H,Nq,dqk] (q or q_low)

@@ -48,6 +48,10 @@ int device_setup(unsigned int** status) {
     int dev;
     int rc = current_device(&dev);
     if (rc) return rc;
+    // Binds the device's primary context to the calling thread (a thread
+    // that has only selected the device, e.g. autograd's worker, may have
+    // none current, and the driver's tensor-map encoder needs one).
+    if (cudaSetDevice(dev) != cudaSuccess) return fail(ADA_ERR_DEVICE, "cudaSetDevice(%d) failed", dev);
     std::lock_guard<std::mutex> lock(g_mu);
     if (g_cc_major[dev] == 0) {
         cudaDeviceProp prop;
@@ -167,6 +171,24 @@ int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int6
     if (rc) return rc;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(width * 2)};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ADA_ERR_LAYOUT, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return ADA_OK;
+}
+
+// 2-D map over a row-major [rows, width] 16-bit matrix whose rows are `ld`
+// elements apart, with a box_rows x 128-byte box and 128-byte swizzle.
+int make_map_rows(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int64_t width, int64_t rows,
+                  int64_t ld, int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int rc = encoder(&enc);
+    if (rc) return rc;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>((rows > 1 ? ld : width) * 2)};
     cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
     cuuint32_t es[2] = {1, 1};
     CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1260,6 +1282,79 @@ int ada_attn_bwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
     L.dv_out = static_cast<float*>(dv->data);
     rc = launch_attn_bwd(L, static_cast<cudaStream_t>(stream));
     return rc ? fail(rc, "backward launch failed: %s", cudaGetErrorString(cudaGetLastError())) : ADA_OK;
+}
+
+int ada_linear(const AdaTensor* x, const AdaTensor* w, const AdaTensor* bias, const AdaTensor* residual,
+               int32_t activation, AdaTensor* y, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if (x == nullptr || w == nullptr || y == nullptr) return fail(ADA_ERR_INVALID, "x, w and y must be non-null");
+    if (x->ndim != 2 || w->ndim != 2 || y->ndim != 2)
+        return fail(ADA_ERR_SHAPE, "x [M,K], w [N,K] and y [M,N] must be 2-D");
+    const int dt = x->dtype;
+    if (dt != ADA_BF16 && dt != ADA_F16) return fail(ADA_ERR_DTYPE, "x must be bf16 or fp16");
+    if (w->dtype != dt || y->dtype != dt) return fail(ADA_ERR_DTYPE, "x, w and y must share one dtype");
+    const int64_t M = x->shape[0], K = x->shape[1], N = w->shape[0];
+    if (M < 0 || K < 0 || N < 0) return fail(ADA_ERR_SHAPE, "negative extent");
+    if (w->shape[1] != K) return fail(ADA_ERR_SHAPE, "w must be [N, K] with K = x.shape[1]");
+    if (y->shape[0] != M || y->shape[1] != N) return fail(ADA_ERR_SHAPE, "y must be [M, N]");
+    if (activation != 0 && activation != 1) return fail(ADA_ERR_INVALID, "activation must be 0 (none) or 1 (gelu)");
+    if (bias != nullptr && bias->data != nullptr) {
+        if (bias->dtype != dt) return fail(ADA_ERR_DTYPE, "bias dtype differs from x");
+        if (bias->ndim != 1 || bias->shape[0] != N || (N > 1 && bias->stride[0] != 1))
+            return fail(ADA_ERR_SHAPE, "bias must be a contiguous [N] vector");
+    }
+    const bool has_r = residual != nullptr && residual->data != nullptr;
+    if (has_r) {
+        if (residual->dtype != dt) return fail(ADA_ERR_DTYPE, "residual dtype differs from x");
+        if (residual->ndim != 2 || residual->shape[0] != M || residual->shape[1] != N)
+            return fail(ADA_ERR_SHAPE, "residual must be [M, N]");
+    }
+    if (M == 0 || N == 0) return ADA_OK;
+    if (K == 0) return fail(ADA_ERR_UNSUPPORTED, "K = 0");
+    if (x->data == nullptr || w->data == nullptr || y->data == nullptr)
+        return fail(ADA_ERR_INVALID, "x, w and y data must be non-null");
+    // TMA: 16-byte aligned bases and row strides, unit inner strides.
+    auto rows_ok = [](const AdaTensor* t) {
+        return aligned16(t->data) && (t->shape[1] <= 1 || t->stride[1] == 1) &&
+               (t->shape[0] <= 1 || (t->stride[0] > 0 && (t->stride[0] * 2) % 16 == 0));
+    };
+    if (!rows_ok(x) || !rows_ok(w))
+        return fail(ADA_ERR_LAYOUT, "x and w need unit column strides, 16-byte aligned bases and row strides");
+    if (N > 1 && y->stride[1] != 1) return fail(ADA_ERR_LAYOUT, "y needs a unit column stride");
+    if (has_r && N > 1 && residual->stride[1] != 1) return fail(ADA_ERR_LAYOUT, "residual needs a unit column stride");
+    if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31))
+        return fail(ADA_ERR_UNSUPPORTED, "extents must be below 2^31");
+    LinearLaunch L{};
+    const CUtensorMapDataType tdt = tma_dtype(dt);
+    if ((rc = make_map_rows(&L.tx, x->data, tdt, K, M, x->stride[0], 128)) ||
+        (rc = make_map_rows(&L.tw, w->data, tdt, K, N, w->stride[0], 256)))
+        return rc;
+    L.bias = (bias != nullptr) ? bias->data : nullptr;
+    L.resid = has_r ? residual->data : nullptr;
+    L.y = y->data;
+    L.M = M;
+    L.N = N;
+    L.K = K;
+    L.ld_y = M > 1 ? y->stride[0] : N;
+    L.ld_r = has_r ? (M > 1 ? residual->stride[0] : N) : 0;
+    L.dtype = dt;
+    L.act = activation;
+    const bool bias_vec = L.bias == nullptr || aligned16(L.bias);
+    const bool r_vec = !has_r || (aligned16(L.resid) && (L.ld_r * 2) % 16 == 0);
+    (void)bias_vec;
+    L.vec = (aligned16(L.y) && (L.ld_y * 2) % 16 == 0 && r_vec) ? 1 : 0;
+    // Output (and residual) tiles through TMA when their rows are 16-byte aligned.
+    L.tma_io = L.vec;
+    if (L.tma_io) {
+        if ((rc = make_map_rows(&L.ty, L.y, tdt, N, M, L.ld_y, 32))) return rc;
+        if (has_r && (rc = make_map_rows(&L.tr, L.resid, tdt, N, M, L.ld_r, 32))) return rc;
+    }
+    L.status = st;
+    L.timeout_ns = wait_timeout_ns();
+    rc = launch_linear_tc(L, static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "linear launch failed: %s", cudaGetErrorString(cudaGetLastError())) : ADA_OK;
 }
 
 int ada_debug_bounded_wait(uint64_t timeout_ns, void* stream) {

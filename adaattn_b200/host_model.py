@@ -13,6 +13,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
+from . import core
 from .attention import AdaAttention
 
 
@@ -31,9 +32,22 @@ class TransformerBlock(nn.Module):
                                 nn.Linear(ff_dim, embed_dim), nn.Dropout(dropout))
 
     def forward(self, x: torch.Tensor, attention_mask=None) -> torch.Tensor:
+        if self._fused(x):
+            # The same sums with the residual adds, the biases and the GELU in
+            # the epilogues of the tensor-core layers (core.linear).
+            x = self.norm1(self.attention.forward_with_residual(x, attention_mask))
+            up, down = self.ff[0], self.ff[3]
+            f = core.linear(x, up.weight, up.bias, activation="gelu")
+            return self.norm2(core.linear(f, down.weight, down.bias, residual=x))
         attn_out, _ = self.attention(x, x, x, attention_mask=attention_mask)
         x = self.norm1(x + attn_out)
         return self.norm2(x + self.ff(x))
+
+    def _fused(self, x: torch.Tensor) -> bool:
+        dropout_off = not self.training or all(
+            m.p == 0 for m in (self.ff[2], self.ff[4], self.attention.resid_dropout))
+        return (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and dropout_off
+                and isinstance(self.ff[1], nn.GELU) and self.ff[1].approximate == "none")
 
 
 class AdaptiveTransformer(nn.Module):

@@ -246,6 +246,22 @@ int         ada_rsvd(const AdaTensor* a, const AdaTensor* omega, int32_t rank, i
                      AdaTensor* u, AdaTensor* s, AdaTensor* vh,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* The module's dense layers on the tensor cores: y = act(x w^T + bias) (+ residual),
+ * replacing the nn.Linear calls on either side of the attention path: the
+ * q/k/v projections (src/adaattn/attention/adaattn.py:411-418, stacked into
+ * one [3E, E] weight for self-attention) and out_proj (:457), plus the
+ * host transformer block's feed-forward and residual sums
+ * (examples/transformer_integration.py:33-58).
+ *   x [M, K], w [N, K] (nn.Linear's weight), y [M, N]: 2-D views, one dtype
+ *     (bf16 or fp16), unit column strides; x and w with 16-byte aligned bases
+ *     and row strides (so K is a multiple of 8).
+ *   bias [N] contiguous or NULL; residual [M, N] or NULL.
+ *   activation 0: none, 1: GELU, erf form (nn.GELU()).
+ * Rounds like the PyTorch ops it replaces: the Linear's output to the dtype,
+ * then the GELU's, then the residual sum's; products accumulate in fp32. */
+int         ada_linear(const AdaTensor* x, const AdaTensor* w, const AdaTensor* bias,
+                       const AdaTensor* residual, int32_t activation, AdaTensor* y, void* stream);
+
 /* Test hook for failure detection: launches one block that waits on a device
  * barrier nothing ever signals, bounded by `timeout_ns`; the wait gives up,
  * records ADA_ERR_TIMEOUT in the status word and the kernel returns normally. */

@@ -37,7 +37,7 @@ __all__ = [
     "rsvd_sketch", "E4M3_MAX", "FP8_TILE",
     "kernel_flash_attention_forward", "kernel_adaptive_attention_forward",
     "compute_entropy", "estimate_effective_rank", "determine_target_ranks",
-    "attention_grads", "attention_grads_from_out",
+    "attention_grads", "attention_grads_from_out", "linear_layer",
 ]
 
 FP32, FP16, BF16, FP8, AUTO = 0, 1, 2, 3, 4
@@ -578,3 +578,36 @@ def attention_grads(q, k, v, dout, scale: float, causal: bool, attention_mask=No
     out = torch.matmul(torch.softmax(z, dim=-1), vd)
     out.backward(dout.double())
     return qd.grad, kd.grad, vd.grad, (wd.grad if wd is not None else None)
+
+
+# --------------------------------------------------------------------------
+# The dense layers on either side of the path: nn.Linear (the module's q/k/v
+# projections, adaattn.py:411-418, and out_proj, :457) and the host block's
+# feed-forward / residual sums (examples/transformer_integration.py:33-58).
+# --------------------------------------------------------------------------
+
+def linear_layer(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                 activation: Optional[str] = None, residual: Optional[torch.Tensor] = None
+                 ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """y = act(x Wᵀ + b) + r with PyTorch's rounding points for 16-bit tensors:
+    the Linear's result is rounded to x's dtype, then GELU's (erf form,
+    nn.GELU()), then the residual sum's. The products are summed exactly
+    (float64), so the only difference from a device result is the device's
+    fp32 accumulation order.
+
+    Returns (y in x's dtype, the float64 sum x Wᵀ + b before any rounding,
+    for error bounds).
+    """
+    dt = x.dtype
+    h64 = x.double() @ weight.double().t()
+    if bias is not None:
+        h64 = h64 + bias.double()
+    y = h64.to(dt)
+    if activation == "gelu":
+        y = F.gelu(y.float()).to(dt)
+    elif activation is not None:
+        raise ValueError(f"unknown activation {activation!r}")
+    if residual is not None:
+        y = (y.float() + residual.float()).to(dt)
+    return y, h64
+
