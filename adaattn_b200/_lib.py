@@ -29,11 +29,11 @@ ADA_ERR = {
 }
 ADA_ERR_TIMEOUT = -7
 
-ADA_F32, ADA_F16, ADA_BF16, ADA_E4M3, ADA_BOOL, ADA_I32, ADA_I64 = range(7)
+ADA_F32, ADA_F16, ADA_BF16, ADA_E4M3, ADA_BOOL, ADA_I32, ADA_I64, ADA_F64 = range(8)
 DTYPE_CODE = {
     torch.float32: ADA_F32, torch.float16: ADA_F16, torch.bfloat16: ADA_BF16,
     torch.float8_e4m3fn: ADA_E4M3, torch.bool: ADA_BOOL, torch.uint8: ADA_BOOL,
-    torch.int32: ADA_I32, torch.int64: ADA_I64,
+    torch.int32: ADA_I32, torch.int64: ADA_I64, torch.float64: ADA_F64,
 }
 SUMMARY_LEN = 12
 
@@ -84,6 +84,8 @@ _SIGNATURES = {
     "ada_attn_bwd": (c_int32, [_T, _T, _T, _T, _T, _T, c_void_p, c_int32, POINTER(AdaFwdParams),
                                _T, _T, _T, c_void_p, c_size_t, c_void_p]),
     "ada_linear": (c_int32, [_T, _T, _T, _T, c_int32, _T, c_void_p]),
+    "ada_layer_norm": (c_int32, [_T, _T, _T, c_float, _T, c_void_p]),
+    "ada_record_statistics": (c_int32, [c_void_p, _T, _T, _T, c_void_p]),
     "ada_rsvd_workspace_bytes": (c_size_t, [_T, _T, c_int32]),
     "ada_rsvd": (c_int32, [_T, _T, c_int32, c_int32, _T, _T, _T, c_void_p, c_size_t, c_void_p]),
 }

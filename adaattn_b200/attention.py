@@ -364,11 +364,9 @@ class AdaAttention(nn.Module):
 
     # -- statistics (adaattn.py:476-486, :506-544) ------------------------------
     def _record(self, table: core.DecisionTable) -> None:
-        s = table.summary
-        total = s[9]
-        self._call_count += 1
-        self._low_rank_calls += (s[4] / total).to(self._low_rank_calls.dtype)
-        self._precision_distribution += (s[5:9] / total).to(self._precision_distribution.dtype)
+        # One launch, on the device, in the buffers' dtypes (ada_record_statistics).
+        core.record_statistics(table.summary, self._call_count, self._low_rank_calls,
+                               self._precision_distribution)
 
     def _record_static(self) -> None:
         self._call_count += 1

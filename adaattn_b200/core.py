@@ -339,6 +339,48 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     return _unflat(y, x.shape[:-1])
 
 
+def layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+               eps: float = 1e-5) -> torch.Tensor:
+    """``nn.LayerNorm`` over the last dimension (``ada_layer_norm``), the host
+    block's norms (examples/transformer_integration.py:44-45, 81): fp32 mean
+    and variance, the result rounded once to x's dtype (bf16 or fp16). No
+    autograd: callers that need gradients use ``nn.LayerNorm`` itself."""
+    _require_cuda(x, weight, bias)
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"layer_norm runs in bf16 or fp16, got {x.dtype}")
+    e = x.shape[-1]
+    for t in (weight, bias):
+        if t is not None and (t.dtype != x.dtype or tuple(t.shape) != (e,)):
+            raise ShapeError(f"weight and bias must be [{e}] in {x.dtype}")
+    x2 = _rows(x)
+    y = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
+    w = weight.contiguous() if weight is not None else None
+    b = bias.contiguous() if bias is not None else None
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.ada_layer_norm(_lib.tensor(x2), _lib.tensor(w) if w is not None else None,
+                                _lib.tensor(b) if b is not None else None, float(eps), _lib.tensor(y),
+                                _lib.stream_ptr(x.device))
+    _lib.check(rc, "ada_layer_norm")
+    return y.view(x.shape)
+
+
+def record_statistics(summary: torch.Tensor, call_count: torch.Tensor, low_rank_calls: torch.Tensor,
+                      precision_distribution: torch.Tensor) -> None:
+    """Add one call's decision summary to the module's running statistics in
+    place, on the device and without a host sync (``ada_record_statistics``;
+    adaattn.py:486-498): call_count += 1, low_rank_calls += n_lowrank / total,
+    precision_distribution += counts / total, each ratio in its buffer's dtype."""
+    _require_cuda(summary, call_count, low_rank_calls, precision_distribution)
+    if summary.dtype != torch.float32 or not summary.is_contiguous() or summary.numel() < _lib.SUMMARY_LEN:
+        raise ShapeError("summary must be a contiguous float32 decision summary")
+    lib = _lib.load()
+    with torch.cuda.device(summary.device):
+        rc = lib.ada_record_statistics(summary.data_ptr(), _lib.tensor(call_count), _lib.tensor(low_rank_calls),
+                                       _lib.tensor(precision_distribution), _lib.stream_ptr(summary.device))
+    _lib.check(rc, "ada_record_statistics")
+
+
 def _host_params(scale, causal, static_precision, static_low_rank, fp8_mode):
     p = _lib.AdaFwdParams()
     p.scale = float(scale)

@@ -241,7 +241,7 @@ int launch_fmha_simt(const SimtLaunch& L, cudaStream_t stream);
 // --- dense layers (tcgen05 GEMM with a fused epilogue) --------------------------
 struct LinearLaunch {
     CUtensorMap tx;      // x [M, K], 64-column x 128-row boxes, 128-byte swizzle
-    CUtensorMap tw;      // W [N, K], 64-column x 256-row boxes
+    CUtensorMap tw;      // W [N, K], 64-column x 128-row boxes (half of a 256-column tile per CTA)
     CUtensorMap ty;      // y [M, N], 64-column x 32-row boxes (stores), when tma_io
     CUtensorMap tr;      // resid [M, N], 64-column x 32-row boxes (loads), when tma_io and resid
     const void* bias;    // [N] or null
@@ -257,6 +257,21 @@ struct LinearLaunch {
     uint64_t timeout_ns;
 };
 int launch_linear_tc(const LinearLaunch& L, cudaStream_t stream);
+
+// --- LayerNorm and running statistics ------------------------------------------
+struct NormLaunch {
+    const void* x;       // [M, E] rows at ld_x
+    const void* weight;  // [E] or null
+    const void* bias;    // [E] or null
+    void* y;             // [M, E] rows at ld_y
+    int64_t M, ld_x, ld_y;
+    int E;
+    int dtype;           // ADA_BF16 or ADA_F16
+    float eps;
+};
+int launch_layer_norm(const NormLaunch& L, cudaStream_t stream);
+int launch_record_stats(const float* summary, int64_t* call_count, void* low_rank_calls, int lr_dtype,
+                        void* precision_distribution, int pd_dtype, cudaStream_t stream);
 
 // --- attention backward (fp32 CUDA cores) --------------------------------------
 struct BwdLaunch {

@@ -1329,7 +1329,7 @@ int ada_linear(const AdaTensor* x, const AdaTensor* w, const AdaTensor* bias, co
     LinearLaunch L{};
     const CUtensorMapDataType tdt = tma_dtype(dt);
     if ((rc = make_map_rows(&L.tx, x->data, tdt, K, M, x->stride[0], 128)) ||
-        (rc = make_map_rows(&L.tw, w->data, tdt, K, N, w->stride[0], 256)))
+        (rc = make_map_rows(&L.tw, w->data, tdt, K, N, w->stride[0], 128)))
         return rc;
     L.bias = (bias != nullptr) ? bias->data : nullptr;
     L.resid = has_r ? residual->data : nullptr;
@@ -1355,6 +1355,69 @@ int ada_linear(const AdaTensor* x, const AdaTensor* w, const AdaTensor* bias, co
     L.timeout_ns = wait_timeout_ns();
     rc = launch_linear_tc(L, static_cast<cudaStream_t>(stream));
     return rc ? fail(rc, "linear launch failed: %s", cudaGetErrorString(cudaGetLastError())) : ADA_OK;
+}
+
+int ada_layer_norm(const AdaTensor* x, const AdaTensor* weight, const AdaTensor* bias, float eps, AdaTensor* y,
+                   void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if (x == nullptr || y == nullptr) return fail(ADA_ERR_INVALID, "x and y must be non-null");
+    if (x->ndim != 2 || y->ndim != 2) return fail(ADA_ERR_SHAPE, "x and y must be 2-D [M, E]");
+    const int dt = x->dtype;
+    if (dt != ADA_BF16 && dt != ADA_F16) return fail(ADA_ERR_DTYPE, "x must be bf16 or fp16");
+    if (y->dtype != dt) return fail(ADA_ERR_DTYPE, "y dtype differs from x");
+    const int64_t M = x->shape[0], E = x->shape[1];
+    if (y->shape[0] != M || y->shape[1] != E) return fail(ADA_ERR_SHAPE, "y must be [M, E]");
+    const AdaTensor* params[2] = {weight, bias};
+    for (const AdaTensor* t : params) {
+        if (t == nullptr || t->data == nullptr) continue;
+        if (t->dtype != dt) return fail(ADA_ERR_DTYPE, "weight and bias must have x's dtype");
+        if (t->ndim != 1 || t->shape[0] != E || (E > 1 && t->stride[0] != 1) || !aligned16(t->data))
+            return fail(ADA_ERR_LAYOUT, "weight and bias must be contiguous, 16-byte aligned [E] vectors");
+    }
+    if (M == 0) return ADA_OK;
+    if (E <= 0 || E % 8 != 0 || E > 2048) return fail(ADA_ERR_UNSUPPORTED, "E must be a multiple of 8 in [8, 2048]");
+    auto rows_ok = [](const AdaTensor* t) {
+        return t->data != nullptr && aligned16(t->data) && t->stride[1] == 1 &&
+               (t->shape[0] <= 1 || (t->stride[0] * 2) % 16 == 0);
+    };
+    if (!rows_ok(x) || !rows_ok(y))
+        return fail(ADA_ERR_LAYOUT, "x and y need unit column strides and 16-byte aligned rows");
+    NormLaunch L{};
+    L.x = x->data;
+    L.y = y->data;
+    L.weight = (weight != nullptr) ? weight->data : nullptr;
+    L.bias = (bias != nullptr) ? bias->data : nullptr;
+    L.M = M;
+    L.E = static_cast<int>(E);
+    L.ld_x = M > 1 ? x->stride[0] : E;
+    L.ld_y = M > 1 ? y->stride[0] : E;
+    L.dtype = dt;
+    L.eps = eps;
+    rc = launch_layer_norm(L, static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "layer-norm launch failed") : ADA_OK;
+}
+
+int ada_record_statistics(const float* summary, AdaTensor* call_count, AdaTensor* low_rank_calls,
+                          AdaTensor* precision_distribution, void* stream) {
+    unsigned int* st;
+    int rc = device_setup(&st);
+    if (rc) return rc;
+    if (summary == nullptr || call_count == nullptr || low_rank_calls == nullptr || precision_distribution == nullptr ||
+        call_count->data == nullptr || low_rank_calls->data == nullptr || precision_distribution->data == nullptr)
+        return fail(ADA_ERR_INVALID, "null argument");
+    if (call_count->dtype != ADA_I64) return fail(ADA_ERR_DTYPE, "call_count must be int64");
+    auto float_ok = [](int d) { return d == ADA_F32 || d == ADA_F16 || d == ADA_BF16 || d == ADA_F64; };
+    if (!float_ok(low_rank_calls->dtype) || !float_ok(precision_distribution->dtype))
+        return fail(ADA_ERR_DTYPE, "statistics buffers must be floating point");
+    if (precision_distribution->ndim != 1 || precision_distribution->shape[0] != 4 ||
+        precision_distribution->stride[0] != 1)
+        return fail(ADA_ERR_SHAPE, "precision_distribution must be a contiguous [4] vector");
+    rc = launch_record_stats(summary, static_cast<int64_t*>(call_count->data), low_rank_calls->data,
+                             low_rank_calls->dtype, precision_distribution->data, precision_distribution->dtype,
+                             static_cast<cudaStream_t>(stream));
+    return rc ? fail(rc, "statistics launch failed") : ADA_OK;
 }
 
 int ada_debug_bounded_wait(uint64_t timeout_ns, void* stream) {

@@ -17,6 +17,17 @@ from . import core
 from .attention import AdaAttention
 
 
+def _norm(norm: nn.LayerNorm, x: torch.Tensor) -> torch.Tensor:
+    """The block's LayerNorm: one ada_layer_norm launch for 16-bit inputs
+    without autograd, nn.LayerNorm (with its backward) otherwise."""
+    if (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and norm.elementwise_affine
+            and norm.weight.dtype == x.dtype and len(norm.normalized_shape) == 1
+            and x.shape[-1] % 8 == 0 and x.shape[-1] <= 2048
+            and not (torch.is_grad_enabled() and (x.requires_grad or norm.weight.requires_grad))):
+        return core.layer_norm(x, norm.weight, norm.bias, norm.eps)
+    return norm(x)
+
+
 class TransformerBlock(nn.Module):
     """examples/transformer_integration.py:12-58."""
 
@@ -35,10 +46,10 @@ class TransformerBlock(nn.Module):
         if self._fused(x):
             # The same sums with the residual adds, the biases and the GELU in
             # the epilogues of the tensor-core layers (core.linear).
-            x = self.norm1(self.attention.forward_with_residual(x, attention_mask))
+            x = _norm(self.norm1, self.attention.forward_with_residual(x, attention_mask))
             up, down = self.ff[0], self.ff[3]
             f = core.linear(x, up.weight, up.bias, activation="gelu")
-            return self.norm2(core.linear(f, down.weight, down.bias, residual=x))
+            return _norm(self.norm2, core.linear(f, down.weight, down.bias, residual=x))
         attn_out, _ = self.attention(x, x, x, attention_mask=attention_mask)
         x = self.norm1(x + attn_out)
         return self.norm2(x + self.ff(x))
@@ -89,7 +100,7 @@ class AdaptiveTransformer(nn.Module):
         x = self.embed_dropout(self.token_embedding(input_ids) + self.position_embedding(pos))
         for block in self.blocks:
             x = block(x, attention_mask=attention_mask)
-        return self._logits(self.norm(x))
+        return self._logits(_norm(self.norm, x))
 
     def _logits(self, h: torch.Tensor) -> torch.Tensor:
         """The tied head. A vocabulary that is not a multiple of 64 (50257)

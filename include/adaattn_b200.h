@@ -52,6 +52,7 @@ extern "C" {
 #define ADA_BOOL  4   /* one byte per element, nonzero = keep */
 #define ADA_I32   5
 #define ADA_I64   6
+#define ADA_F64   7   /* statistics buffers only */
 
 /* ---- precision codes: the reference's _precision_distribution order
  *      (src/adaattn/attention/adaattn.py:480-485) plus AUTO, which computes
@@ -261,6 +262,23 @@ int         ada_rsvd(const AdaTensor* a, const AdaTensor* omega, int32_t rank, i
  * then the GELU's, then the residual sum's; products accumulate in fp32. */
 int         ada_linear(const AdaTensor* x, const AdaTensor* w, const AdaTensor* bias,
                        const AdaTensor* residual, int32_t activation, AdaTensor* y, void* stream);
+
+/* LayerNorm over the last dimension of x [M, E] (bf16 or fp16, unit column
+ * stride, 16-byte aligned rows, E a multiple of 8 and <= 2048), weight and
+ * bias [E] contiguous in x's dtype (either may be NULL): the host block's
+ * nn.LayerNorm (examples/transformer_integration.py:44-45, 81) in fp32
+ * arithmetic, rounded once. y [M, E] may alias x. */
+int         ada_layer_norm(const AdaTensor* x, const AdaTensor* weight, const AdaTensor* bias,
+                           float eps, AdaTensor* y, void* stream);
+
+/* Adds one call's decision summary (ada_analyze's `summary`) to the module's
+ * running statistics buffers like adaattn.py:486-498: call_count (int64
+ * scalar) += 1, low_rank_calls (scalar) += n_lowrank / total, and
+ * precision_distribution[4] += counts / total, each ratio cast to its
+ * buffer's dtype (fp32, fp16, bf16 or ADA_F64) and added in that dtype. */
+int         ada_record_statistics(const float* summary, AdaTensor* call_count,
+                                  AdaTensor* low_rank_calls, AdaTensor* precision_distribution,
+                                  void* stream);
 
 /* Test hook for failure detection: launches one block that waits on a device
  * barrier nothing ever signals, bounded by `timeout_ns`; the wait gives up,
