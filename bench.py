@@ -14,7 +14,9 @@ attention; the NCCL all-gather of the outputs is timed separately afterwards
 (``--scaling weak`` gives every rank its own B8 H32 job instead). The time of
 a step is the maximum over ranks; rank 0 prints one JSON line, with every
 rank's kernel time. A second leg times the GPT-2-small-shaped decoder with
-AdaAttention in every layer, its batch of 16 split over the ranks.
+AdaAttention in every layer, its batch of 16 split over the ranks. On one
+GPU a third leg times the E4M3 variant of the same attention workload beside
+a dense FP8 GEMM peak measured in the same process.
 
 --impl reference times the reference algorithm's CPU implementation (the
 oracle's restatement of AdaAttention._compute_dense_attention) on the host
@@ -272,6 +274,66 @@ def gpt2_leg(dev, world, rank, barrier, steps=10):
             "attention_precision_layer0": stats["precision_distribution"]}
 
 
+def fp8_leg(dev, w, steps=20):
+    """The E4M3 variant on the same workload (static precision FP8, E4M3
+    quantisation of q, k, v included in every step), beside a dense FP8 GEMM
+    peak measured in this process (cuBLASLt e4m3 x e4m3 -> bf16, 8192^3,
+    best of 10): the denominator for the E4M3 kernel's tensor-core fraction."""
+    from adaattn_b200 import PrecisionMode, attention_forward
+    from adaattn_b200.workloads import make_qkv
+    n = 8192
+    a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    one = torch.ones((), device=dev)
+    peak = None
+    try:
+        for _ in range(3):
+            torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        best = float("inf")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(10):
+            e0.record()
+            torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        peak = 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    except (RuntimeError, AttributeError) as e:  # no FP8 GEMM in this torch build
+        peak_err = str(e).splitlines()[0][:120]
+    del a, b
+    q, k, v = make_qkv(w, seed=1000, device=str(dev))
+    out = torch.empty(q.shape, dtype=w.dtype, device=dev)
+    scale = 1.0 / math.sqrt(w.head_dim)
+
+    def step():
+        attention_forward(q, k, v, scale=scale, causal=w.causal, static_precision=PrecisionMode.FP8,
+                          out=out)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    tflops = w.dense_flops() / (ms * 1e-3) / 1e12
+    res = {"workload": f"dense causal attention B{w.batch} H{w.heads} N{w.seq} D{w.head_dim}, "
+                       "precision forced FP8 (E4M3 operands, per-tile scales; quantisation in the step)",
+           "ms_per_step": ms, "tflops": tflops, "steps": steps}
+    if peak is not None:
+        res["fp8_gemm_peak_tflops"] = peak
+        res["frac_of_fp8_peak"] = tflops / peak
+    else:
+        res["fp8_gemm_peak_tflops"] = None
+        res["fp8_peak_unavailable"] = peak_err
+    del q, k, v, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -283,6 +345,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gpt2", action="store_true", help="skip the GPT-2-small leg")
+    ap.add_argument("--no-fp8", action="store_true", help="skip the E4M3 leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="profiling only: smaller batch than the B8 workload")
     ap.add_argument("--heads", type=int, default=None,
@@ -417,6 +480,7 @@ def main():
     torch.cuda.empty_cache()
 
     gpt2 = None if args.no_gpt2 else gpt2_leg(dev, world, rank, barrier)
+    fp8 = fp8_leg(dev, workload) if (world == 1 and not args.no_fp8) else None
 
     if world > 1:
         dist.barrier()
@@ -454,6 +518,8 @@ def main():
             line["allgather_outputs_ms"] = allgather_ms
         if gpt2 is not None:
             line["gpt2_small"] = gpt2
+        if fp8 is not None:
+            line["fp8_e4m3"] = fp8
         if not args.no_cpu_baseline and world == 1:  # the host-core baseline is an N=1 figure
             v_cpu, cores, desc = cpu_sample(w)
             line["cpu_baseline"] = {"value": v_cpu, "unit": "TFLOP/s", "cores": cores,
