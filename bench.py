@@ -228,7 +228,8 @@ def gpt2_leg(dev, world, rank, barrier, steps=10):
     """GPT-2-small-shaped decoder with AdaAttention in every layer (12 layers,
     E768, H12, FF3072, seq 1024, batch 16, weights N(0, 0.02), bf16): forward
     tokens/s, the batch split over the ranks (replicated weights, no
-    collective in the forward)."""
+    collective in the forward), each step one replay of the forward captured
+    in a CUDA graph."""
     from adaattn_b200 import AdaAttention
     from adaattn_b200.host_model import AdaptiveTransformer
     from adaattn_b200.shard import shard_range
@@ -252,12 +253,27 @@ def gpt2_leg(dev, world, rank, barrier, steps=10):
 
     for _ in range(3):
         step()
+    torch.cuda.synchronize()
+    # One forward captured in a CUDA graph (no host synchronisation inside:
+    # decisions, statistics and workspaces live on the device) and replayed:
+    # at a few sequences per GPU the eager forward is bound by the host's
+    # launch sequence, not by the GPU.
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        step()
+        with torch.cuda.graph(graph, stream=side):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    for _ in range(3):
+        graph.replay()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-        step()
+        graph.replay()
     e1.record()
     barrier()
     ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
@@ -266,11 +282,12 @@ def gpt2_leg(dev, world, rank, barrier, steps=10):
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item()) / steps
     stats = model.get_attention_statistics()[0]
+    del graph
     del model
     return {"workload": f"gpt2_small decoder B{c['batch']} N{c['seq']} E{c['embed_dim']} "
                         f"H{c['num_heads']} L{c['num_layers']} bf16, batch split over {world} GPU(s)",
             "tokens_per_s": c["batch"] * c["seq"] / (ms * 1e-3), "ms_per_forward": ms,
-            "sequences_per_gpu": hi - lo, "steps": steps,
+            "sequences_per_gpu": hi - lo, "steps": steps, "cuda_graph": True,
             "attention_precision_layer0": stats["precision_distribution"]}
 
 
