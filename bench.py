@@ -288,12 +288,13 @@ def gpt2_leg(dev, world, rank, barrier, steps=10):
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item()) / steps
     stats = model.get_attention_statistics()[0]
-    del graph
+    used_graph = graph is not None
+    del run, graph
     del model
     return {"workload": f"gpt2_small decoder B{c['batch']} N{c['seq']} E{c['embed_dim']} "
                         f"H{c['num_heads']} L{c['num_layers']} bf16, batch split over {world} GPU(s)",
             "tokens_per_s": c["batch"] * c["seq"] / (ms * 1e-3), "ms_per_forward": ms,
-            "sequences_per_gpu": hi - lo, "steps": steps, "cuda_graph": graph is not None,
+            "sequences_per_gpu": hi - lo, "steps": steps, "cuda_graph": used_graph,
             "attention_precision_layer0": stats["precision_distribution"]}
 
 
