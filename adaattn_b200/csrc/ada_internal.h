@@ -116,6 +116,8 @@ struct PrepLaunch {
     uint32_t f16_mask;    // ...of which these compute in fp16 (the rest bf16)
     int direct_ok;        // dense heads already in their compute dtype are read in place
     int mixed16;          // dense FP16 heads of bf16 inputs read q, k in place: only v is cast
+    int v_direct;         // 16-bit heads whose compute dtype is the inputs' (or FP16 of bf16 inputs, converted
+                          // in the attention kernel) read v in place: no cast copy of v
     void* ws16_q;
     void* ws16_k;
     void* ws16_v;
@@ -196,6 +198,8 @@ struct TcLaunch {
     int elt;          // 0 f16, 1 bf16, 2 e4m3; FP32 heads (P as fp16 hi + lo, fp16 V): 3 fp16 q/k, 4 bf16 q/k;
                       // 5 FP16 heads of bf16 inputs: bf16 q/k in place, fp16 P and V
     int dqk, dv;      // operand widths (64 or 128)
+    int v_convert;    // elt 0 / 5 only: 1 = tv maps the bf16 v itself and the kernel converts each
+                      // value block to fp16 in shared memory before P·V (no cast copy of v)
     int64_t B, H, Nq, Nk;
     int dv_out;       // real value width stored
     void* out;

@@ -239,6 +239,7 @@ struct Plan {
     int fp8_mode;
     uint32_t tc16_mask, f16_mask, fp8_mask, fp32_mask;
     bool direct_ok;
+    bool v_direct;       // v itself is TMA-readable at the padded width (the kernels read it in place)
     int dqk_dense, dqk_low, dv_pad;
     int64_t ld16_qk, ld16_v;
     bool need16, need32, need8;
@@ -324,6 +325,7 @@ int build_plan(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, const
     // A rank wider than a 64-wide head pads V to 128 as well: the kernels
     // pair a 128-wide Q K^T only with a 128-wide P V.
     P->dv_pad = P->dqk_low > pad_width(P->D) ? P->dqk_low : pad_width(P->D);
+    P->v_direct = P->direct_ok && P->dv_pad == P->D;
     P->ld16_qk = P->dqk_dense > P->dqk_low ? P->dqk_dense : P->dqk_low;
     P->ld16_v = P->dv_pad;
     P->need16 = false;
@@ -723,6 +725,7 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
     pl.f16_mask = P.f16_mask;
     pl.direct_ok = P.direct_ok ? 1 : 0;
     pl.mixed16 = (P.direct_ok && P.in_dtype == ADA_BF16) ? 1 : 0;
+    pl.v_direct = P.v_direct ? 1 : 0;
     pl.ld16_qk = P.ld16_qk;
     pl.ld16_v = P.ld16_v;
     pl.dqk_dense = P.dqk_dense;
@@ -742,7 +745,12 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
         pl.ws16_q = ws + P.off16q;
         pl.ws16_k = ws + P.off16k;
         pl.ws16_v = ws + P.off16v;
-        if (proj_tc || !P.low_possible) {
+        // bf16 inputs read in place: q/k of dense heads directly (FP16 heads
+        // too), q_low/k_low from the tensor-core projection, v directly or
+        // converted to fp16 inside the attention kernel -- nothing to cast.
+        const bool nothing_to_cast = P.in_dtype == ADA_BF16 && P.v_direct && (proj_tc || !P.low_possible);
+        if (nothing_to_cast) {
+        } else if (proj_tc || !P.low_possible) {
             if ((rc = launch_cast16(pl, proj_tc ? 1 : 0, s))) return fail(rc, "operand cast launch failed");
         } else if ((rc = launch_prep16(pl, s))) {
             return fail(rc, "prep16 launch failed");
@@ -880,6 +888,8 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
             const bool direct = !low && cd == P.in_dtype && P.direct_ok;
             // FP16 heads of bf16 inputs: bf16 q, k in place, v from the cast region
             const bool mixed = !low && cd == ADA_F16 && P.in_dtype == ADA_BF16 && P.direct_ok;
+            // v of 16-bit heads read in place (bf16 v of FP16 heads converted in the kernel)
+            const bool v_in_place = P.v_direct && (cd == P.in_dtype || (cd == ADA_F16 && P.in_dtype == ADA_BF16));
             if (mixed) {
                 L.elt = 5;
                 L.dqk = static_cast<int>(P.D);
@@ -887,9 +897,15 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
                 const CUtensorMapDataType bf = tma_dtype(ADA_BF16);
                 const int64_t lv = P.ld16_v;
                 if ((rc = make_map(&L.tq, q->data, bf, 2, P.D, P.Nq, P.H, P.B, q->stride[2], q->stride[1], q->stride[0])) ||
-                    (rc = make_map(&L.tk, k->data, bf, 2, P.D, P.Nk, P.H, P.B, k->stride[2], k->stride[1], k->stride[0])) ||
-                    (rc = make_map(&L.tv, ws + P.off16v, dt, 2, L.dv, P.Nk, P.H, P.B, lv, P.Nk * lv, P.H * P.Nk * lv)))
+                    (rc = make_map(&L.tk, k->data, bf, 2, P.D, P.Nk, P.H, P.B, k->stride[2], k->stride[1], k->stride[0])))
                     return rc;
+                if (v_in_place) {
+                    L.v_convert = 1;
+                    rc = make_map(&L.tv, v->data, bf, 2, P.D, P.Nk, P.H, P.B, v->stride[2], v->stride[1], v->stride[0]);
+                } else {
+                    rc = make_map(&L.tv, ws + P.off16v, dt, 2, L.dv, P.Nk, P.H, P.B, lv, P.Nk * lv, P.H * P.Nk * lv);
+                }
+                if (rc) return rc;
             } else if (direct) {
                 L.dqk = static_cast<int>(P.D);
                 L.dv = static_cast<int>(P.D);
@@ -902,9 +918,16 @@ int ada_attn_fwd(const AdaTensor* q, const AdaTensor* k, const AdaTensor* v, con
                 L.dv = P.dv_pad;
                 const int64_t l = P.ld16_qk, lv = P.ld16_v;
                 if ((rc = make_map(&L.tq, ws + P.off16q, dt, 2, L.dqk, P.Nq, P.H, P.B, l, P.Nq * l, P.H * P.Nq * l)) ||
-                    (rc = make_map(&L.tk, ws + P.off16k, dt, 2, L.dqk, P.Nk, P.H, P.B, l, P.Nk * l, P.H * P.Nk * l)) ||
-                    (rc = make_map(&L.tv, ws + P.off16v, dt, 2, L.dv, P.Nk, P.H, P.B, lv, P.Nk * lv, P.H * P.Nk * lv)))
+                    (rc = make_map(&L.tk, ws + P.off16k, dt, 2, L.dqk, P.Nk, P.H, P.B, l, P.Nk * l, P.H * P.Nk * l)))
                     return rc;
+                if (v_in_place) {
+                    L.v_convert = cd != P.in_dtype ? 1 : 0;
+                    rc = make_map(&L.tv, v->data, tma_dtype(P.in_dtype), 2, P.D, P.Nk, P.H, P.B, v->stride[2],
+                                  v->stride[1], v->stride[0]);
+                } else {
+                    rc = make_map(&L.tv, ws + P.off16v, dt, 2, L.dv, P.Nk, P.H, P.B, lv, P.Nk * lv, P.H * P.Nk * lv);
+                }
+                if (rc) return rc;
             }
             // 16-bit output through TMA stores when every row start is
             // 16-byte aligned (the epilogue stages the tile in shared memory).

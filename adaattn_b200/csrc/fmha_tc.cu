@@ -20,8 +20,11 @@
 //   warp 8           TMA producer (Q tiles per item, double buffered; then
 //                    K_j, V_j through the ring).
 //   warp 9           TMEM allocation and the single-thread MMA issuer.
-//   warps 10-11      idle (they complete the third warpgroup, which hands
-//                    its registers to the softmax warpgroups).
+//   warps 10-11      FP16 heads of bf16 inputs (v_convert): convert each
+//                    value block from bf16 to fp16 in place in shared memory
+//                    between its TMA load and its P·V; otherwise idle (they
+//                    complete the third warpgroup, which hands its registers
+//                    to the softmax warpgroups).
 // The two query tiles ping-pong: while one tile's softmax runs, the tensor
 // core works on the other tile's products. Across items the producer and the
 // MMA issuer run ahead, so the next item's first products overlap this item's
@@ -48,6 +51,8 @@ constexpr int kOtherRegs = 88;
 // Threads that read each broadcast work item: the MMA issuer and the 256
 // softmax threads.
 constexpr int kItemConsumers = 1 + 256;
+// Threads of warps 10-11, the value-block converters.
+constexpr int kConvThreads = 64;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kOtherRegs <= kThreadsTc * kLaunchRegs,
               "register split exceeds the launch pool");
 // Dynamic shared memory budget: 227 KB per CTA minus alignment slack and the
@@ -111,6 +116,7 @@ struct __align__(8) TcBarriers {
     int64_t item_q[4];
     uint64_t kv_full[8];
     uint64_t kv_empty[8];
+    uint64_t v_ready[8];     // value block converted to fp16 (v_convert)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -228,6 +234,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // bf16 value blocks converted to fp16 in shared memory (FP16 P·V variants only).
+    const bool vconv = (ELT == 0 || ELT == 5) && L.v_convert != 0;
 
     // A launch for a branch and precision that no head chose ends here,
     // before any setup (the adaptive path launches every variant it may need).
@@ -250,11 +258,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
         mbar_init(smem_u32(&bars->teardown), 1);
         for (int i = 0; i < 4; ++i) {
             mbar_init(smem_u32(&bars->item_full[i]), 1);
-            mbar_init(smem_u32(&bars->item_empty[i]), kItemConsumers);
+            mbar_init(smem_u32(&bars->item_empty[i]), kItemConsumers + (vconv ? kConvThreads : 0));
         }
         for (int s = 0; s < C::NSTAGE; ++s) {
             mbar_init(smem_u32(&bars->kv_full[s]), 1);
             mbar_init(smem_u32(&bars->kv_empty[s]), 1);
+            mbar_init(smem_u32(&bars->v_ready[s]), kConvThreads);
         }
         bars->abort_flag = 0;
         fence_mbar_init();
@@ -340,6 +349,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             const uint32_t sKVa = smem_u32(sKV);
             uint32_t qi = 0, kvi = 0, ic = 0;
             uint32_t pc[2] = {0u, 0u};  // P blocks consumed per tile
+            uint32_t vpar = 0;          // per ring slot: parity of its v_ready phase
             bool ok = true;
             int64_t it;
             auto issue_s = [&](int t, uint32_t qbuf, uint32_t stage) {
@@ -386,8 +396,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
                 for (int j = 0; ok && j < w.nblk; ++j) {
                     const uint32_t iv = kvi + 2 * j + 1;
                     const uint32_t sv = iv % C::NSTAGE;
-                    ok = mbar_wait(smem_u32(&bars->kv_full[sv]), (iv / C::NSTAGE) & 1u, abort_flag, tmo,
+                    // v_ready completes only for the value blocks of a slot (a slot
+                    // also takes key blocks when the ring length is odd): its
+                    // parity is tracked per slot.
+                    const uint32_t vph = vconv ? ((vpar >> sv) & 1u) : ((iv / C::NSTAGE) & 1u);
+                    ok = mbar_wait(smem_u32(vconv ? &bars->v_ready[sv] : &bars->kv_full[sv]), vph, abort_flag, tmo,
                                    status);
+                    vpar ^= vconv ? (1u << sv) : 0u;
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t ik = kvi + 2 * j + 2;
@@ -429,6 +444,42 @@ __global__ void __launch_bounds__(kThreadsTc, 1) fmha_tc_kernel(const __grid_con
             teardown_wait(smem_u32(&bars->teardown), 0, tmo, status);
         }
         __syncwarp();
+      } else if (vconv) {
+        // ---------------- value-block converters (warps 10-11) ----------------
+        // Each value block, once TMA has landed it, is rewritten in place as
+        // fp16 (same positions in the swizzled layout: the conversion is
+        // elementwise), then handed to the MMA issuer. Rounding: round to
+        // nearest, overflow to infinity, as a cast of v to fp16 does.
+        if constexpr (ELT == 0 || ELT == 5) {
+            const int ct = static_cast<int>(threadIdx.x) - 320;
+            uint32_t ic = 0, kvi = 0;
+            bool ok = true;
+            int64_t it;
+            while (ok && take_item(bars, ic, it, abort_flag, tmo, status)) {
+                const Item w = decode_item(L, it, n_qtp, nkb);
+                for (int j = 0; ok && j < w.nblk; ++j) {
+                    const uint32_t iv = kvi + 2 * j + 1;
+                    const uint32_t sv = iv % C::NSTAGE;
+                    ok = mbar_wait(smem_u32(&bars->kv_full[sv]), (iv / C::NSTAGE) & 1u, abort_flag, tmo, status);
+                    if (!ok) break;
+                    uint4* blk = reinterpret_cast<uint4*>(sKV + sv * C::STAGE_BYTES);
+#pragma unroll 4
+                    for (int c = ct; c < C::V_BYTES / 16; c += kConvThreads) {
+                        const uint4 x = blk[c];
+                        const uint32_t wi[4] = {x.x, x.y, x.z, x.w};
+                        uint32_t wo[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            wo[e] = pack_f16x2(__uint_as_float(wi[e] << 16), __uint_as_float(wi[e] & 0xFFFF0000u));
+                        blk[c] = make_uint4(wo[0], wo[1], wo[2], wo[3]);
+                    }
+                    // The tensor core reads the block through the async proxy.
+                    fence_proxy_async_smem();
+                    mbar_arrive(smem_u32(&bars->v_ready[sv]));
+                }
+                kvi += 2 * w.nblk;
+            }
+        }
       }
     } else {
         regs_increase<kSoftmaxRegs>();

@@ -202,7 +202,9 @@ __global__ void __launch_bounds__(kThreads) cast16_kernel(const __grid_constant_
                       reinterpret_cast<uint16_t*>(L.ws16_k) + bh * L.Nk * L.ld16_qk, L.ld16_qk, L.dqk_dense, cd,
                       vec_k != 0);
     }
-    if (row0 < L.Nk)
+    // v read in place by the attention kernel (converted there for FP16 heads of bf16 inputs)
+    const bool v_in_place = L.v_direct && (cd == L.in_dtype || (cd == ADA_F16 && L.in_dtype == ADA_BF16));
+    if (row0 < L.Nk && !v_in_place)
         cast_rows(L.v, L.in_dtype, L.vs, b, h, row0, L.Nk, D,
                   reinterpret_cast<uint16_t*>(L.ws16_v) + bh * L.Nk * L.ld16_v, L.ld16_v, L.dv_pad, cd, vec_v != 0);
 }
