@@ -59,7 +59,8 @@ DENSE_CASES = [
     (torch.bfloat16, O.BF16, 128, 333, 64),
     (torch.float16, O.FP16, 128, 256, 256),
     (torch.float16, O.FP16, 64, 130, 130),
-    (torch.bfloat16, O.FP16, 128, 256, 256),   # cast in the prep kernel
+    (torch.bfloat16, O.FP16, 128, 256, 256),   # bf16 q/k in place, v converted in the kernel
+    (torch.bfloat16, O.FP16, 64, 200, 200),    # the same at D = 64 (the decoder's heads)
     (torch.float32, O.FP16, 64, 256, 256),
     (torch.float32, O.BF16, 128, 192, 192),
     (torch.float32, O.AUTO, 64, 128, 128),
@@ -101,6 +102,7 @@ LOW_CASES = [
     (torch.float16, O.FP16, 64, 32, 200),
     (torch.bfloat16, O.BF16, 128, 128, 256),
     (torch.bfloat16, O.FP16, 128, 100, 190),
+    (torch.bfloat16, O.FP16, 64, 32, 200),     # v read in place, converted to fp16 in the kernel
     (torch.float16, O.FP32, 128, 64, 140),
     (torch.bfloat16, O.BF16, 64, 100, 128),    # r_pad 128 > D: SIMT projection
     (torch.bfloat16, O.FP32, 128, 100, 150),   # pipelined CUDA-core path, bf16 V
@@ -123,6 +125,35 @@ def test_low_rank_static(case, causal, cuda_device):
     for h in range(2):
         check_head(out[:, h:h + 1], q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], prec, True,
                    scale, causal, w_down=w, label=f"h{h}")
+
+
+@pytest.mark.parametrize("low", [False, True])
+def test_fp16_heads_of_bf16_inputs_overflowing_v(low, cuda_device):
+    """FP16 heads of bf16 inputs convert v to fp16 inside the attention
+    kernel; a bf16 value beyond fp16's range becomes infinite there, as the
+    reference's cast of v to fp16 makes it (adaattn.py:297-299): the same
+    outputs turn infinite or NaN, and every other output keeps the FP16 bar."""
+    q, k, v = _inputs(1, 2, 300, 300, 128, torch.bfloat16, seed=11)
+    v[0, 0, 7, 5] = 1.0e5     # +inf in fp16
+    v[0, 1, 40, 9] = -3.0e5   # -inf in fp16
+    w = _w_down(128, 64, torch.bfloat16) if low else None
+    out, scale = _run(q, k, v, O.FP16, low, False, cuda_device, w=w)
+    for h in range(2):
+        qh, kh, vh = q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1]
+        if low:
+            ref = O.low_rank_attention(qh, kh, vh, w, O.FP16, scale, False)
+        else:
+            ref = O.dense_attention(qh, kh, vh, O.FP16, scale, False)
+        got = out[:, h:h + 1]
+        assert torch.equal(torch.isnan(got), torch.isnan(ref))
+        assert torch.equal(torch.isinf(got), torch.isinf(ref))
+        assert int(torch.isinf(ref).sum()) > 0
+        fin = torch.isfinite(ref)
+        err = (got[fin].float() - ref[fin].float()).abs().max().item()
+        mag = ref[fin].float().abs().max().item()
+        bar = 2e-3 * max(1.0, mag) + half_spacing(got.dtype, mag)
+        record(f"overflow_v/low{int(low)}/h{h}", "FP16", err, bar)
+        assert err <= bar
 
 
 @pytest.mark.parametrize("causal", [False, True])
