@@ -257,6 +257,8 @@ struct LinearLaunch {
     int act;             // 0: none, 1: GELU (erf form)
     int vec;             // 16-byte aligned rows of y and resid
     int tma_io;          // y (and resid) through per-warp shared-memory tiles and TMA
+    int n_fastest;       // tile order: 1 = the N tiles of one x row block run side by side (x read from
+                         // HBM once, W kept in L2), 0 = the M tiles of one W block (W read once)
     unsigned int* status;
     uint64_t timeout_ns;
 };

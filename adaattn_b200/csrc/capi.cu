@@ -1356,6 +1356,7 @@ int ada_linear(const AdaTensor* x, const AdaTensor* w, const AdaTensor* bias, co
         return rc;
     L.bias = (bias != nullptr) ? bias->data : nullptr;
     L.resid = has_r ? residual->data : nullptr;
+    L.n_fastest = M >= N ? 1 : 0;  // x (M x K) is the larger operand: read it once
     L.y = y->data;
     L.M = M;
     L.N = N;

@@ -6,8 +6,9 @@
 //
 // x [M, K] and W [N, K] are 16-bit (both the same type), rows K-contiguous, so
 // both operands are K-major. CTA pairs (clusters of two, one CTA per SM,
-// persistent) walk 256 x 256 output tiles, M-fastest (the pairs running
-// together share one 256-row block of W; x stays in L2). Each tile is one
+// persistent) walk 256 x 256 output tiles, N-fastest when x is the larger
+// operand (the pairs running together share one 256-row block of x, which
+// is read from HBM once; W stays in L2), else M-fastest. Each tile is one
 // chain of cta_group::2 tcgen05 MMAs (M = 256, N = 256, K = 16): CTA r of the
 // pair loads rows 128 r .. +127 of the tile's x block and rows 128 r .. +127
 // of its W block, 64-column K blocks through a 5-stage shared-memory ring
@@ -93,6 +94,17 @@ __device__ __noinline__ void epilogue_chunk_edge(const float* accv, const float*
     }
 }
 
+// Output tile t -> (M tile, N tile): the N tiles of one x row block side by
+// side (n_fastest), or the M tiles of one W column block side by side. The
+// pairs running together then share one operand block through L2, and the
+// operand that is larger in HBM is the one read from it once.
+__device__ __forceinline__ int tile_m(int64_t t, int n_m, int n_n, bool n_fastest) {
+    return static_cast<int>(n_fastest ? t / n_n : t % n_m);
+}
+__device__ __forceinline__ int tile_n(int64_t t, int n_m, int n_n, bool n_fastest) {
+    return static_cast<int>(n_fastest ? t % n_n : t / n_m);
+}
+
 // The barrier at this shared-memory offset in both CTAs of the pair receives
 // one arrival when the issuing thread's products so far have completed.
 __device__ __forceinline__ void commit_both(uint32_t bar) {
@@ -115,6 +127,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
     const int n_n = static_cast<int>((L.N + kBN - 1) / kBN);
     const int64_t n_tiles = static_cast<int64_t>(n_m) * n_n;
     const int n_k = static_cast<int>((L.K + kBK - 1) / kBK);
+    const bool nfast = L.n_fastest != 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -150,7 +163,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
             uint32_t kc = 0;
             bool ok = true;
             for (int64_t t = pair; ok && t < n_tiles; t += n_pairs) {
-                const int mt = static_cast<int>(t % n_m), nt = static_cast<int>(t / n_m);
+                const int mt = tile_m(t, n_m, n_n, nfast), nt = tile_n(t, n_m, n_n, nfast);
                 const int xrow = mt * kPairM + static_cast<int>(rank) * kBM;
                 const int wrow = nt * kBN + static_cast<int>(rank) * kBNh;
                 for (int kb = 0; kb < n_k; ++kb, ++kc) {
@@ -238,7 +251,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
         // The even CTA's acc_empty barriers, where this warp reports a drained buffer.
         const uint32_t acc_empty0 = mapa_shared(smem_u32(&bars->acc_empty[0]), 0);
         for (int64_t t = pair; ok && t < n_tiles; t += n_pairs, ++tc) {
-            const int mt = static_cast<int>(t % n_m), nt = static_cast<int>(t / n_m);
+            const int mt = tile_m(t, n_m, n_n, nfast), nt = tile_n(t, n_m, n_n, nfast);
             const uint32_t ab = tc & 1u;
             // This warp's 128 bias values, lane l holding columns l, l+32, l+64,
             // l+96 (zero past N); broadcast by shuffles below.
