@@ -24,18 +24,22 @@
 //   t = round(acc + b)                   nn.Linear's output in the inputs' dtype
 //   t = round(gelu(t))                   nn.GELU (erf form), when asked
 //   t = round(t + r)                     the residual sum, when asked
-// Warp roles (320 threads per CTA): warp 0 TMA producer, warp 1 TMEM
-// allocation and (even CTA) MMA issue, warps 2-9 epilogue (warp w reads TMEM
-// lanes 32 (w mod 4) .. +31, one output row per thread, and columns
-// 128 ((w - 2) / 4) .. +127 of the tile). Every wait is bounded (ada::mbar_wait):
-// a timeout raises the CTA's abort flag and ADA_ERR_TIMEOUT in the status word.
+// Warp roles (576 threads per CTA): warp 0 TMA producer, warp 1 TMEM
+// allocation and (even CTA) MMA issue, warps 2-17 epilogue in two groups of
+// eight, group g draining the tiles of accumulator buffer g (every other
+// tile), so two tiles' epilogues run at once and hide each other's latency
+// (a GELU epilogue is as long as a K = 768 main loop). Warp w reads TMEM lanes
+// 32 (w mod 4) .. +31, one output row per thread, and columns
+// 128 (((w - 2) mod 8) / 4) .. +127 of its tile. Every wait is bounded
+// (ada::mbar_wait): a timeout raises the CTA's abort flag and ADA_ERR_TIMEOUT
+// in the status word.
 #include "ada_common.cuh"
 #include "ada_internal.h"
 
 namespace ada {
 namespace {
 
-constexpr int kLinThreads = 320;
+constexpr int kLinThreads = 576;  // warps 0-1 TMA and MMA, warps 2-17 two epilogue groups
 constexpr int kBM = 128;                      // rows of the tile per CTA (256 per pair)
 constexpr int kPairM = 256;
 constexpr int kBN = 256;                      // columns of the tile
@@ -46,7 +50,7 @@ constexpr int kABytes = kBM * kBK * 2;        // 16 KB
 constexpr int kBBytes = kBNh * kBK * 2;       // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kStgBytes = 32 * 128;          // one 32-row x 64-column output tile
-constexpr int kLinSmem = kStages * kStageBytes + 16 * kStgBytes + 1024 + 256;  // two tiles per epilogue warp
+constexpr int kLinSmem = kStages * kStageBytes + 16 * kStgBytes + 1024 + 256;  // one tile per epilogue warp
 
 struct __align__(8) LinBarriers {
     uint64_t full[kStages];
@@ -54,7 +58,7 @@ struct __align__(8) LinBarriers {
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
     uint64_t teardown;
-    uint64_t rfull[8];  // per epilogue warp: its residual tile has landed
+    uint64_t rfull[16];  // per epilogue warp: its residual tile has landed
     // full[] and acc_empty[] are used on the even CTA only (the odd CTA's TMA
     // loads and epilogue warps count on the even CTA's copies).
     uint32_t tmem_base;
@@ -139,7 +143,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
             mbar_init(smem_u32(&bars->acc_empty[a]), 16);  // one arrival per epilogue warp of the pair
         }
         mbar_init(smem_u32(&bars->teardown), 1);
-        for (int w = 0; w < 8; ++w) mbar_init(smem_u32(&bars->rfull[w]), 1);
+        for (int w = 0; w < 16; ++w) mbar_init(smem_u32(&bars->rfull[w]), 1);
         bars->abort_flag = 0;
         fence_mbar_init();
     }
@@ -236,13 +240,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
         // it with TMA (rows past M, columns past N clipped). A residual tile
         // arrives in the same slot by TMA and is overwritten in place.
         const int quad = warp & 3;
-        const int half = (warp - 2) >> 2;
         const int ew = warp - 2;
+        const int grp = ew >> 3;          // accumulator buffer this warp drains
+        const int half = (ew & 7) >> 2;
         const uint32_t lane_bits = static_cast<uint32_t>(quad * 32) << 16;
         const int act = L.act;
         const bool has_r = L.resid != nullptr;
         const bool tma_io = L.tma_io != 0;
-        uint8_t* stg_w = sstg + ew * 2 * kStgBytes;  // this warp's two slots
+        uint8_t* stg_w = sstg + ew * kStgBytes;  // this warp's slot
         const uint32_t rbar = smem_u32(&bars->rfull[ew]);
         uint32_t rph = 0;
         const int64_t N = L.N;
@@ -251,8 +256,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
         // The even CTA's acc_empty barriers, where this warp reports a drained buffer.
         const uint32_t acc_empty0 = mapa_shared(smem_u32(&bars->acc_empty[0]), 0);
         for (int64_t t = pair; ok && t < n_tiles; t += n_pairs, ++tc) {
-            const int mt = tile_m(t, n_m, n_n, nfast), nt = tile_n(t, n_m, n_n, nfast);
             const uint32_t ab = tc & 1u;
+            if (static_cast<int>(ab) != grp) continue;  // the other group's tile
+            const int mt = tile_m(t, n_m, n_n, nfast), nt = tile_n(t, n_m, n_n, nfast);
             // This warp's 128 bias values, lane l holding columns l, l+32, l+64,
             // l+96 (zero past N); broadcast by shuffles below.
             float breg[4];
@@ -272,10 +278,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
                 // A tile that lies wholly past M or N (the odd CTA's rows of a
                 // last, partial pair tile) is neither loaded nor stored.
                 const bool live = row0 < L.M && col0 < N;
-                // Chunk c2 uses slot c2: the store that last read it is the
-                // one before the other slot's, so at most one store may still
-                // be reading when this chunk starts.
-                uint8_t* stg = stg_w + c2 * kStgBytes;
+                // One slot per warp: the previous chunk's store must have read
+                // it before this chunk (or its residual tile) is written.
+                uint8_t* stg = stg_w;
                 const uint32_t stg_a = smem_u32(stg);
                 uint32_t r0[32], r1[32];
                 tmem_ld32(tacc + c2 * 64, r0);
@@ -285,7 +290,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kLinThreads, 1)
                     // free once this warp's previous store has read it; then the
                     // residual tile may land in it.
                     if (lane == 0) {
-                        bulk_wait_group_read1();
+                        bulk_wait_group_read0();
                         if (has_r && live) {
                             mbar_arrive_expect_tx(rbar, kStgBytes);
                             tma_load_2d(stg_a, &L.tr, rbar, static_cast<int>(col0), static_cast<int>(row0));
