@@ -215,6 +215,10 @@ class AdaAttention(nn.Module):
         # base.py:466-492
         if not self.config.enable_nan_check:
             return
+        if tensor.is_cuda and torch.cuda.is_current_stream_capturing():
+            # A forward being captured into a CUDA graph cannot read the
+            # device; the check runs on eager forwards only.
+            return
         if torch.isnan(tensor).any():
             raise NumericalError(f"NaN values detected in {name}. "
                                  "Consider using higher precision or gradient clipping.")
