@@ -218,6 +218,8 @@ struct TcLaunch {
     const float* v_scale;  // e4m3 and FP32 heads: [B,H]
     int64_t nt_q, nt_k;
     int* work_counter;  // zeroed work-item counter (dynamic scheduling), or nullptr (static striding)
+    int head_group;     // heads per scheduling group (>= 1): items are handed out group by group,
+                        // heaviest query-tile pair first across the group's heads
     unsigned int* status;
     uint64_t timeout_ns;
 };
